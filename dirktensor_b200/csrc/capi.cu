@@ -1,0 +1,746 @@
+// extern "C" layer of the B200 attention hot path (declared in
+// include/dirktensor_b200.h).  The whole library is this one translation unit:
+// the kernel headers are included below.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/dirktensor_b200.h"
+#include "dt_common.cuh"
+#include "flash_fwd.cuh"
+#include "gemm.cuh"
+#include "prologue.cuh"
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxSeqLen = 8192;  // model_config.h:4 (RoPE table length)
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+#define DT_CUDA(call)                                                                                    \
+    do {                                                                                                 \
+        cudaError_t e_ = (call);                                                                         \
+        if (e_ != cudaSuccess)                                                                           \
+            return fail(e_ == cudaErrorMemoryAllocation ? DT_ERR_OUT_OF_MEMORY : DT_ERR_CUDA, "%s: %s (%s:%d)", \
+                        #call, cudaGetErrorString(e_), __FILE__, __LINE__);                              \
+    } while (0)
+
+#define DT_TRY(expr)              \
+    do {                          \
+        int s_ = (expr);          \
+        if (s_ != DT_OK) return s_; \
+    } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Tensor maps through the driver entry point (no link-time libcuda dependency)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode(EncodeTiledFn* out) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&fn), cudaEnableDefault, &q);
+        if (err == cudaSuccess && q != cudaDriverEntryPointSuccess) err = cudaErrorNotSupported;
+    });
+    if (err != cudaSuccess || fn == nullptr)
+        return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(err));
+    *out = fn;
+    return DT_OK;
+}
+
+// bf16 [B, T, H, D] token-major -> 4-D map (D, H, T, B), box 64 x 1 x 128 x 1, 128 B swizzle.
+int make_map_bthd(CUtensorMap* m, const void* base, int B, int T, int H, int D) {
+    EncodeTiledFn enc;
+    DT_TRY(get_encode(&enc));
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+    const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2, (cuuint64_t)T * H * D * 2};
+    const cuuint32_t box[4] = {64, 1, 128, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled(BTHD) failed: %d", (int)r);
+    return DT_OK;
+}
+
+// bf16 row-major [rows, K] -> 2-D map (K, rows), box 64 x box_rows, 128 B swizzle.
+int make_map_2d(CUtensorMap* m, const void* base, long long rows, int K, int box_rows) {
+    EncodeTiledFn enc;
+    DT_TRY(get_encode(&enc));
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled(2D) failed: %d", (int)r);
+    return DT_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Per-device state: kernel attributes, RoPE tables, host-API staging buffers
+// ---------------------------------------------------------------------------
+struct DevState {
+    bool attrs = false;
+    float* sin_t = nullptr;
+    float* cos_t = nullptr;
+    float rope_theta = 0.f;
+    cudaStream_t stream = nullptr;  // host-buffer entry points
+    void* stage = nullptr;
+    size_t stage_bytes = 0;
+};
+std::mutex g_mu;
+DevState g_dev[64];
+
+constexpr size_t kFlashSmem = sizeof(dt::flash::Smem) + 1024;
+constexpr size_t kGemmSmem = sizeof(dt::gemm::Smem) + 1024;
+
+int current_device(int* dev) {
+    DT_CUDA(cudaGetDevice(dev));
+    if (*dev < 0 || *dev >= 64) return fail(DT_ERR_UNSUPPORTED, "device index %d out of range", *dev);
+    return DT_OK;
+}
+
+// Called with g_mu held.
+int ensure_attrs(int dev) {
+    DevState& s = g_dev[dev];
+    if (s.attrs) return DT_OK;
+    cudaDeviceProp prop;
+    DT_CUDA(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10)
+        return fail(DT_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
+                    prop.major, prop.minor);
+    DT_CUDA(cudaFuncSetAttribute(dt::flash::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kFlashSmem));
+    DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kGemmSmem));
+    s.attrs = true;
+    return DT_OK;
+}
+
+int prepare_device(int* dev_out) {
+    int dev;
+    DT_TRY(current_device(&dev));
+    std::lock_guard<std::mutex> lk(g_mu);
+    DT_TRY(ensure_attrs(dev));
+    *dev_out = dev;
+    return DT_OK;
+}
+
+void rope_tables_host(std::vector<float>& sin_t, std::vector<float>& cos_t, int max_seq, int head_dim,
+                      double theta) {
+    // compute_rope_buffers (OlmoAttention.cpp:18-36): inv_freq in double, angle
+    // p * inv_freq[j mod half], sin/cos in double, cast to float.
+    const int half = head_dim / 2;
+    sin_t.resize((size_t)max_seq * head_dim);
+    cos_t.resize((size_t)max_seq * head_dim);
+    std::vector<double> inv(half);
+    for (int i = 0; i < half; ++i) inv[i] = 1.0 / std::pow(theta, (double)(2 * i) / (double)head_dim);
+    for (int p = 0; p < max_seq; ++p)
+        for (int j = 0; j < head_dim; ++j) {
+            const double a = (double)p * inv[j % half];
+            sin_t[(size_t)p * head_dim + j] = (float)std::sin(a);
+            cos_t[(size_t)p * head_dim + j] = (float)std::cos(a);
+        }
+}
+
+int ensure_rope(int dev, float theta, const float** sin_t, const float** cos_t) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState& s = g_dev[dev];
+    if (s.sin_t == nullptr || s.rope_theta != theta) {
+        std::vector<float> hs, hc;
+        rope_tables_host(hs, hc, kMaxSeqLen, 128, (double)theta);
+        const size_t bytes = hs.size() * sizeof(float);
+        if (s.sin_t == nullptr) {
+            DT_CUDA(cudaMalloc(&s.sin_t, bytes));
+            DT_CUDA(cudaMalloc(&s.cos_t, bytes));
+        }
+        DT_CUDA(cudaMemcpy(s.sin_t, hs.data(), bytes, cudaMemcpyHostToDevice));
+        DT_CUDA(cudaMemcpy(s.cos_t, hc.data(), bytes, cudaMemcpyHostToDevice));
+        s.rope_theta = theta;
+    }
+    *sin_t = s.sin_t;
+    *cos_t = s.cos_t;
+    return DT_OK;
+}
+
+// Host-API staging buffer of at least `bytes` on `dev` (called with g_mu held).
+int ensure_stage(int dev, size_t bytes, void** out, cudaStream_t* stream) {
+    DevState& s = g_dev[dev];
+    if (s.stream == nullptr) DT_CUDA(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+    if (s.stage_bytes < bytes) {
+        if (s.stage) DT_CUDA(cudaFree(s.stage));
+        s.stage = nullptr;
+        s.stage_bytes = 0;
+        DT_CUDA(cudaMalloc(&s.stage, bytes));
+        s.stage_bytes = bytes;
+    }
+    *out = s.stage;
+    *stream = s.stream;
+    return DT_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+int launch_cast(const float* src, void* dst, long long n, cudaStream_t st) {
+    if (n == 0) return DT_OK;
+    const long long n4 = n / 4;
+    const int threads = 256;
+    long long blocks = (n4 + threads - 1) / threads;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    dt::elem::cast_f32_bf16_kernel<<<(unsigned)blocks, threads, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                                         reinterpret_cast<uint2*>(dst), n4);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int launch_cast3(const float* a, const float* b, const float* c, void* da, void* db, void* dc, long long n,
+                 cudaStream_t st) {
+    if (n == 0) return DT_OK;
+    dt::elem::Cast3 args;
+    args.src[0] = reinterpret_cast<const float4*>(a);
+    args.src[1] = reinterpret_cast<const float4*>(b);
+    args.src[2] = reinterpret_cast<const float4*>(c);
+    args.dst[0] = reinterpret_cast<uint2*>(da);
+    args.dst[1] = reinterpret_cast<uint2*>(db);
+    args.dst[2] = reinterpret_cast<uint2*>(dc);
+    const long long n4 = n / 4;
+    const int threads = 256;
+    long long blocks = (n4 + threads - 1) / threads;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    dt::elem::cast3_f32_bf16_kernel<<<dim3((unsigned)blocks, 3), threads, 0, st>>>(args, n4);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
+                 float* m, float* l, const int* seq_lens, int B, int T, int H, float scale, int causal,
+                 cudaStream_t st) {
+    if ((long long)B * T * H == 0) return DT_OK;
+    CUtensorMap mq, mk, mv;
+    DT_TRY(make_map_bthd(&mq, q, B, T, H, 128));
+    DT_TRY(make_map_bthd(&mk, k, B, T, H, 128));
+    DT_TRY(make_map_bthd(&mv, v, B, T, H, 128));
+    dt::flash::Params p;
+    p.B = B;
+    p.T = T;
+    p.H = H;
+    p.nblk = (T + 255) / 256;
+    p.causal = causal ? 1 : 0;
+    p.scale = scale;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = o;
+    p.out_bf16 = o_bf16;
+    p.out_row_stride = o_row_stride;
+    p.m_out = m;
+    p.l_out = l;
+    p.seq_lens = seq_lens;
+    const long long grid = (long long)p.nblk * B * H;
+    if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
+    dt::flash::flash_fwd_kernel<<<(unsigned)grid, dt::flash::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N, int K, long long ldc,
+                cudaStream_t st) {
+    if (M == 0 || N == 0) return DT_OK;
+    CUtensorMap ma, mb;
+    DT_TRY(make_map_2d(&ma, A, M, K, dt::gemm::kBM));
+    DT_TRY(make_map_2d(&mb, Bm, N, K, dt::gemm::kBN));
+    dt::gemm::Params p;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.C = C;
+    p.ldc = ldc;
+    p.c_bf16 = c_bf16;
+    dim3 grid((N + dt::gemm::kBN - 1) / dt::gemm::kBN, (M + dt::gemm::kBM - 1) / dt::gemm::kBM);
+    dt::gemm::gemm_bf16_tn_kernel<<<grid, dt::gemm::kThreads, kGemmSmem, st>>>(ma, mb, p);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int launch_prologue(const float* q, const float* k, const float* v, long long ld_in, const float* qg,
+                    const float* kg, const float* sin_t, const float* cos_t, void* qo, void* ko, void* vo, int B,
+                    int T, float eps, cudaStream_t st) {
+    const long long M = (long long)B * T;
+    if (M == 0) return DT_OK;
+    dt::elem::PrologueParams p;
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.ld_in = ld_in;
+    p.q_gain = qg;
+    p.k_gain = kg;
+    p.sin_t = sin_t;
+    p.cos_t = cos_t;
+    p.qo = reinterpret_cast<__nv_bfloat16*>(qo);
+    p.ko = reinterpret_cast<__nv_bfloat16*>(ko);
+    p.vo = reinterpret_cast<__nv_bfloat16*>(vo);
+    p.T = T;
+    p.eps = eps;
+    if (M > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "too many rows");
+    dt::elem::qk_norm_rope_kernel<<<(unsigned)M, dt::elem::kPrologueThreads, 0, st>>>(p);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int check_flash_shape(int B, int T, int H, int D) {
+    if (B < 0 || T < 0 || H < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape B=%d T=%d H=%d", B, T, H);
+    if (D != 128) return fail(DT_ERR_UNSUPPORTED, "head_dim %d unsupported (must be 128)", D);
+    return DT_OK;
+}
+
+int read_device_error(bool* had) {
+    unsigned code = 0, info = 0;
+    DT_CUDA(cudaMemcpyFromSymbol(&code, dt::g_dev_error, sizeof(code)));
+    *had = code != 0;
+    if (code) {
+        DT_CUDA(cudaMemcpyFromSymbol(&info, dt::g_dev_error_info, sizeof(info)));
+        const unsigned zero = 0;
+        DT_CUDA(cudaMemcpyToSymbol(dt::g_dev_error, &zero, sizeof(zero)));
+        return fail(DT_ERR_DEVICE_TIMEOUT, "a kernel wait expired (site 0x%x, parity %u); results are invalid",
+                    code & 0xffu, info);
+    }
+    return DT_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// extern "C"
+// ===========================================================================
+struct dt_attn {
+    int device = 0;
+    int d_model = 0, n_heads = 0;
+    float eps = 1e-6f, theta = 500000.f;
+    __nv_bfloat16* wqkv = nullptr;  // [3*d, d]
+    __nv_bfloat16* wo = nullptr;    // [d, d]
+    float* qg = nullptr;
+    float* kg = nullptr;
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    void* io = nullptr;  // host-API staging: x, y, seq_lens
+    size_t io_bytes = 0;
+    cudaStream_t stream = nullptr;
+};
+
+extern "C" {
+
+const char* dt_last_error(void) { return t_last_error.c_str(); }
+
+int dt_version(void) { return kVersion; }
+
+int dt_check_device_error(void) {
+    DT_CUDA(cudaDeviceSynchronize());
+    bool had;
+    return read_device_error(&had);
+}
+
+size_t dt_flash_fwd_workspace_bytes(int B, int T, int H, int D) {
+    if (B <= 0 || T <= 0 || H <= 0 || D <= 0) return 0;
+    return 3 * align256((size_t)B * T * H * D * 2);
+}
+
+int dt_flash_fwd(const float* q, const float* k, const float* v, float* o, float* softmax_m, float* softmax_l,
+                 int B, int T, int H, int D, float scale, int causal, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (!q || !k || !v || !o) return fail(DT_ERR_INVALID_ARGUMENT, "null q/k/v/o");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v/o must be 16-byte aligned");
+    const size_t need = dt_flash_fwd_workspace_bytes(B, T, H, D);
+    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+        return fail(DT_ERR_INVALID_ARGUMENT, "workspace must be >= %zu bytes and 16-byte aligned", need);
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const long long n = (long long)B * T * H * D;
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    const size_t one = align256((size_t)n * 2);
+    DT_TRY(launch_cast3(q, k, v, ws, ws + one, ws + 2 * one, n, st));
+    return launch_flash(ws, ws + one, ws + 2 * one, o, 0, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H,
+                        scale, causal, st);
+}
+
+int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, float* softmax_m,
+                      float* softmax_l, int B, int T, int H, int D, float scale, int causal) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (!q || !k || !v || !o) return fail(DT_ERR_INVALID_ARGUMENT, "null q/k/v/o");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    const size_t n = (size_t)B * T * H * D;
+    const size_t ns = (size_t)B * T * H;
+    const size_t t_bytes = align256(n * 4), s_bytes = align256(ns * 4);
+    const size_t ws = dt_flash_fwd_workspace_bytes(B, T, H, D);
+    std::lock_guard<std::mutex> lk(g_mu);
+    void* stage;
+    cudaStream_t st;
+    DT_TRY(ensure_stage(dev, 4 * t_bytes + 2 * s_bytes + ws, &stage, &st));
+    uint8_t* base = reinterpret_cast<uint8_t*>(stage);
+    float* dq = reinterpret_cast<float*>(base);
+    float* dk = reinterpret_cast<float*>(base + t_bytes);
+    float* dv = reinterpret_cast<float*>(base + 2 * t_bytes);
+    float* dout = reinterpret_cast<float*>(base + 3 * t_bytes);
+    float* dm = reinterpret_cast<float*>(base + 4 * t_bytes);
+    float* dl = reinterpret_cast<float*>(base + 4 * t_bytes + s_bytes);
+    void* dws = base + 4 * t_bytes + 2 * s_bytes;
+    DT_CUDA(cudaMemcpyAsync(dq, q, n * 4, cudaMemcpyHostToDevice, st));
+    DT_CUDA(cudaMemcpyAsync(dk, k, n * 4, cudaMemcpyHostToDevice, st));
+    DT_CUDA(cudaMemcpyAsync(dv, v, n * 4, cudaMemcpyHostToDevice, st));
+    const long long nn = (long long)n;
+    uint8_t* w = reinterpret_cast<uint8_t*>(dws);
+    const size_t one = align256(n * 2);
+    DT_TRY(launch_cast3(dq, dk, dv, w, w + one, w + 2 * one, nn, st));
+    DT_TRY(launch_flash(w, w + one, w + 2 * one, dout, 0, (long long)H * D, dm, dl, nullptr, B, T, H, scale, causal,
+                        st));
+    DT_CUDA(cudaMemcpyAsync(o, dout, n * 4, cudaMemcpyDeviceToHost, st));
+    if (softmax_m) DT_CUDA(cudaMemcpyAsync(softmax_m, dm, ns * 4, cudaMemcpyDeviceToHost, st));
+    if (softmax_l) DT_CUDA(cudaMemcpyAsync(softmax_l, dl, ns * 4, cudaMemcpyDeviceToHost, st));
+    DT_CUDA(cudaStreamSynchronize(st));
+    bool had;
+    return read_device_error(&had);
+}
+
+int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
+                      float* softmax_m, float* softmax_l, const int* seq_lens, int B, int T, int H, int D,
+                      float scale, int causal, void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (!q || !k || !v || !o) return fail(DT_ERR_INVALID_ARGUMENT, "null q/k/v/o");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v/o must be 16-byte aligned");
+    if (o_row_stride < (long long)H * D || (o_row_stride % 8) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "o_row_stride must be >= H*D and a multiple of 8");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    return launch_flash(q, k, v, o, o_bf16 ? 1 : 0, o_row_stride, softmax_m, softmax_l, seq_lens, B, T, H, scale,
+                        causal, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream) {
+    t_last_error.clear();
+    if (n < 0 || (n % 4) != 0) return fail(DT_ERR_INVALID_ARGUMENT, "n must be a non-negative multiple of 4");
+    if (n == 0) return DT_OK;
+    if (!src || !dst || !aligned16(src) || ((uintptr_t)dst & 7u))
+        return fail(DT_ERR_INVALID_ARGUMENT, "src must be 16-byte and dst 8-byte aligned");
+    return launch_cast(src, dst, n, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, int N, int K, long long ldc,
+                    void* stream) {
+    t_last_error.clear();
+    if (M < 0 || N < 0 || K <= 0 || (K % 8) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "need M,N >= 0 and K > 0 with K %% 8 == 0 (M=%d N=%d K=%d)", M, N, K);
+    if (M == 0 || N == 0) return DT_OK;
+    if (!A || !B || !C || !aligned16(A) || !aligned16(B) || !aligned16(C))
+        return fail(DT_ERR_INVALID_ARGUMENT, "A, B, C must be non-null and 16-byte aligned");
+    if (ldc < N || (ldc % (c_bf16 ? 8 : 4)) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ldc must be >= N and keep rows 16-byte aligned");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    return launch_gemm(A, B, C, c_bf16 ? 1 : 0, M, N, K, ldc, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dt_qk_norm_rope(const float* q, const float* k, const float* v, long long ld_in, const float* q_gain,
+                    const float* k_gain, void* q_out, void* k_out, void* v_out, int B, int T, float eps,
+                    float rope_theta, void* stream) {
+    t_last_error.clear();
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    if (T > kMaxSeqLen) return fail(DT_ERR_INVALID_ARGUMENT, "T=%d exceeds max_seq_len %d", T, kMaxSeqLen);
+    if ((long long)B * T == 0) return DT_OK;
+    if (ld_in < 2048 || (ld_in % 4) != 0) return fail(DT_ERR_INVALID_ARGUMENT, "ld_in must be >= 2048, multiple of 4");
+    if (!q || !k || !v || !q_gain || !k_gain || !q_out || !k_out || !v_out || !aligned16(q) || !aligned16(k) ||
+        !aligned16(v) || !aligned16(q_gain) || !aligned16(k_gain) || !aligned16(q_out) || !aligned16(k_out) ||
+        !aligned16(v_out))
+        return fail(DT_ERR_INVALID_ARGUMENT, "all pointers must be non-null and 16-byte aligned");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    const float *st, *ct;
+    DT_TRY(ensure_rope(dev, rope_theta, &st, &ct));
+    return launch_prologue(q, k, v, ld_in, q_gain, k_gain, st, ct, q_out, k_out, v_out, B, T, eps,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dt_rope_tables(float* sin_out, float* cos_out, int max_seq, int head_dim, float theta) {
+    t_last_error.clear();
+    if (!sin_out || !cos_out || max_seq < 0 || head_dim <= 0 || (head_dim % 2) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "bad rope table arguments");
+    std::vector<float> s, c;
+    rope_tables_host(s, c, max_seq, head_dim, (double)theta);
+    std::memcpy(sin_out, s.data(), s.size() * 4);
+    std::memcpy(cos_out, c.data(), c.size() * 4);
+    return DT_OK;
+}
+
+// ---- attention layer -------------------------------------------------------
+
+static int attn_upload(dt_attn* a, const dt_attn_weights* w) {
+    const int d = w->d_model;
+    const size_t dd = (size_t)d * d;
+    float* stage = nullptr;
+    DT_CUDA(cudaMalloc(&stage, dd * 4));
+    DT_CUDA(cudaMalloc(&a->wqkv, 3 * dd * 2));
+    DT_CUDA(cudaMalloc(&a->wo, dd * 2));
+    DT_CUDA(cudaMalloc(&a->qg, (size_t)d * 4));
+    DT_CUDA(cudaMalloc(&a->kg, (size_t)d * 4));
+    const float* src[4] = {w->q_proj, w->k_proj, w->v_proj, w->o_proj};
+    __nv_bfloat16* dst[4] = {a->wqkv, a->wqkv + dd, a->wqkv + 2 * dd, a->wo};
+    for (int i = 0; i < 4; ++i) {
+        DT_CUDA(cudaMemcpy(stage, src[i], dd * 4, cudaMemcpyHostToDevice));
+        DT_TRY(launch_cast(stage, dst[i], (long long)dd, nullptr));
+        DT_CUDA(cudaDeviceSynchronize());
+    }
+    DT_CUDA(cudaFree(stage));
+    DT_CUDA(cudaMemcpy(a->qg, w->q_norm, (size_t)d * 4, cudaMemcpyHostToDevice));
+    DT_CUDA(cudaMemcpy(a->kg, w->k_norm, (size_t)d * 4, cudaMemcpyHostToDevice));
+    return DT_OK;
+}
+
+int dt_attn_create(const dt_attn_weights* w, int device, dt_attn** out) {
+    t_last_error.clear();
+    if (!w || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (!w->q_proj || !w->k_proj || !w->v_proj || !w->o_proj || !w->q_norm || !w->k_norm)
+        return fail(DT_ERR_INVALID_ARGUMENT, "null weight pointer");
+    if (w->d_model != 2048 || w->n_heads <= 0 || w->d_model % w->n_heads != 0 || w->d_model / w->n_heads != 128)
+        return fail(DT_ERR_UNSUPPORTED, "need d_model 2048 and head_dim 128 (got d_model=%d n_heads=%d)", w->d_model,
+                    w->n_heads);
+    DT_CUDA(cudaSetDevice(device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    dt_attn* a = new dt_attn();
+    a->device = device;
+    a->d_model = w->d_model;
+    a->n_heads = w->n_heads;
+    a->eps = w->eps;
+    a->theta = w->rope_theta;
+    int s = attn_upload(a, w);
+    if (s == DT_OK) {
+        const float *st, *ct;
+        s = ensure_rope(dev, a->theta, &st, &ct);
+    }
+    if (s != DT_OK) {
+        std::string msg = t_last_error;
+        dt_attn_destroy(a);
+        t_last_error = msg;
+        return s;
+    }
+    *out = a;
+    return DT_OK;
+}
+
+// Minimal .npy reader (format version 1.x/2.x/3.x, '<f4', C order), for the
+// checkpoint files OlmoAttention.cpp:39-46 loads with xt::load_npy.
+static int read_npy_f32(const std::string& path, std::vector<float>& data, std::vector<long long>& shape) {
+    FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return fail(DT_ERR_IO, "cannot open %s", path.c_str());
+    unsigned char magic[8];
+    if (std::fread(magic, 1, 8, f) != 8 || std::memcmp(magic, "\x93NUMPY", 6) != 0) {
+        std::fclose(f);
+        return fail(DT_ERR_IO, "%s is not a .npy file", path.c_str());
+    }
+    size_t hlen = 0;
+    if (magic[6] == 1) {
+        unsigned char b[2];
+        if (std::fread(b, 1, 2, f) != 2) { std::fclose(f); return fail(DT_ERR_IO, "%s: truncated", path.c_str()); }
+        hlen = b[0] | (b[1] << 8);
+    } else {
+        unsigned char b[4];
+        if (std::fread(b, 1, 4, f) != 4) { std::fclose(f); return fail(DT_ERR_IO, "%s: truncated", path.c_str()); }
+        hlen = b[0] | (b[1] << 8) | (b[2] << 16) | ((size_t)b[3] << 24);
+    }
+    std::string header(hlen, '\0');
+    if (std::fread(&header[0], 1, hlen, f) != hlen) {
+        std::fclose(f);
+        return fail(DT_ERR_IO, "%s: truncated header", path.c_str());
+    }
+    if (header.find("'descr': '<f4'") == std::string::npos || header.find("'fortran_order': False") == std::string::npos) {
+        std::fclose(f);
+        return fail(DT_ERR_IO, "%s: need little-endian float32 in C order", path.c_str());
+    }
+    shape.clear();
+    const size_t lp = header.find('(', header.find("'shape'"));
+    const size_t rp = header.find(')', lp);
+    if (lp == std::string::npos || rp == std::string::npos) {
+        std::fclose(f);
+        return fail(DT_ERR_IO, "%s: no shape in header", path.c_str());
+    }
+    long long count = 1;
+    for (size_t i = lp + 1; i < rp;) {
+        while (i < rp && (header[i] == ' ' || header[i] == ',')) ++i;
+        if (i >= rp) break;
+        long long v = 0;
+        while (i < rp && header[i] >= '0' && header[i] <= '9') v = v * 10 + (header[i++] - '0');
+        shape.push_back(v);
+        count *= v;
+    }
+    data.resize((size_t)count);
+    const size_t got = std::fread(data.data(), 4, (size_t)count, f);
+    std::fclose(f);
+    if (got != (size_t)count) return fail(DT_ERR_IO, "%s: expected %lld floats, read %zu", path.c_str(), count, got);
+    return DT_OK;
+}
+
+int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_attn** out) {
+    t_last_error.clear();
+    if (!folder || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    const char* names[6] = {"q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"};
+    std::vector<float> buf[6];
+    for (int i = 0; i < 6; ++i) {
+        std::vector<long long> shape;
+        const std::string path = std::string(folder) + "/model.layers." + std::to_string(index) + ".self_attn." +
+                                 names[i] + ".weight.npy";
+        DT_TRY(read_npy_f32(path, buf[i], shape));
+        const bool ok = (i < 4) ? (shape.size() == 2 && shape[0] == 2048 && shape[1] == 2048)
+                                : (shape.size() == 1 && shape[0] == 2048);
+        if (!ok) return fail(DT_ERR_IO, "%s: unexpected shape", path.c_str());
+    }
+    dt_attn_weights w;
+    w.q_proj = buf[0].data();
+    w.k_proj = buf[1].data();
+    w.v_proj = buf[2].data();
+    w.o_proj = buf[3].data();
+    w.q_norm = buf[4].data();
+    w.k_norm = buf[5].data();
+    w.d_model = 2048;
+    w.n_heads = 16;
+    w.eps = 1e-6f;
+    w.rope_theta = 500000.f;
+    return dt_attn_create(&w, device, out);
+}
+
+int dt_attn_destroy(dt_attn* a) {
+    if (!a) return DT_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(a->device);
+    cudaFree(a->wqkv);
+    cudaFree(a->wo);
+    cudaFree(a->qg);
+    cudaFree(a->kg);
+    cudaFree(a->ws);
+    cudaFree(a->io);
+    if (a->stream) cudaStreamDestroy(a->stream);
+    cudaSetDevice(prev);
+    delete a;
+    return DT_OK;
+}
+
+static int attn_workspace(dt_attn* a, long long M, uint8_t** ws) {
+    const size_t need = align256(M * 2048 * 2) * 5 + align256(M * 6144 * 4);
+    if (a->ws_bytes < need) {
+        if (a->ws) DT_CUDA(cudaFree(a->ws));
+        a->ws = nullptr;
+        a->ws_bytes = 0;
+        DT_CUDA(cudaMalloc(&a->ws, need));
+        a->ws_bytes = need;
+    }
+    *ws = reinterpret_cast<uint8_t*>(a->ws);
+    return DT_OK;
+}
+
+int dt_attn_forward(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y, void* stream) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    if (T > kMaxSeqLen) return fail(DT_ERR_INVALID_ARGUMENT, "T=%d exceeds max_seq_len %d", T, kMaxSeqLen);
+    const long long M = (long long)B * T;
+    if (M == 0) return DT_OK;
+    if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(DT_ERR_INVALID_ARGUMENT, "x/y must be 16-byte aligned");
+    int cur;
+    DT_CUDA(cudaGetDevice(&cur));
+    if (cur != a->device) DT_CUDA(cudaSetDevice(a->device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int d = a->d_model;
+    uint8_t* ws;
+    DT_TRY(attn_workspace(a, M, &ws));
+    const size_t act = align256(M * d * 2);
+    void* xb = ws;
+    float* qkv = reinterpret_cast<float*>(ws + act);
+    uint8_t* rest = ws + act + align256(M * 3 * d * 4);
+    void* qb = rest;
+    void* kb = rest + act;
+    void* vb = rest + 2 * act;
+    void* ab = rest + 3 * act;
+    const float *sin_t, *cos_t;
+    DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
+    DT_TRY(launch_cast(x, xb, M * d, st));                                         // x -> bf16
+    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st));         // [q|k|v] = x Wqkv^T
+    DT_TRY(launch_prologue(qkv, qkv + d, qkv + 2 * d, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
+                           st));                                                    // norm + RoPE
+    DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, nullptr, nullptr, seq_lens, B, T, a->n_heads,
+                        1.0f / std::sqrt(128.0f), 1, st));                          // attention
+    DT_TRY(launch_gemm(ab, a->wo, y, 0, (int)M, d, d, d, st));                     // y = a Wo^T
+    return DT_OK;
+}
+
+int dt_attn_forward_host(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    const long long M = (long long)B * T;
+    if (M == 0) return DT_OK;
+    if (!x || !y) return fail(DT_ERR_INVALID_ARGUMENT, "null x/y");
+    DT_CUDA(cudaSetDevice(a->device));
+    if (!a->stream) DT_CUDA(cudaStreamCreateWithFlags(&a->stream, cudaStreamNonBlocking));
+    const size_t xb = align256((size_t)M * a->d_model * 4);
+    const size_t need = 2 * xb + align256((size_t)B * 4);
+    if (a->io_bytes < need) {
+        if (a->io) DT_CUDA(cudaFree(a->io));
+        a->io = nullptr;
+        a->io_bytes = 0;
+        DT_CUDA(cudaMalloc(&a->io, need));
+        a->io_bytes = need;
+    }
+    uint8_t* io = reinterpret_cast<uint8_t*>(a->io);
+    float* dx = reinterpret_cast<float*>(io);
+    float* dy = reinterpret_cast<float*>(io + xb);
+    int* dl = reinterpret_cast<int*>(io + 2 * xb);
+    DT_CUDA(cudaMemcpyAsync(dx, x, (size_t)M * a->d_model * 4, cudaMemcpyHostToDevice, a->stream));
+    if (seq_lens) DT_CUDA(cudaMemcpyAsync(dl, seq_lens, (size_t)B * 4, cudaMemcpyHostToDevice, a->stream));
+    DT_TRY(dt_attn_forward(a, dx, B, T, seq_lens ? dl : nullptr, dy, a->stream));
+    DT_CUDA(cudaMemcpyAsync(y, dy, (size_t)M * a->d_model * 4, cudaMemcpyDeviceToHost, a->stream));
+    DT_CUDA(cudaStreamSynchronize(a->stream));
+    bool had;
+    return read_device_error(&had);
+}
+
+}  // extern "C"

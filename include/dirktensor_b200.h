@@ -1,0 +1,132 @@
+/*
+ * dirktensor_b200 -- C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Drop-in boundary for DirkTensor's attention layer.  Each entry point names
+ * the reference interface it replaces (file:line in the DirkTensor tree).
+ * Plain pointers and sizes only; no C++ or torch types cross this boundary.
+ * Nothing throws: every call returns a status code (DT_OK == 0) and
+ * dt_last_error() gives a message for the calling thread.
+ *
+ * Layouts (as in the reference):
+ *   activations  [B, T, H, D] or [B, T, d_model] row-major fp32 (d_model = H*D)
+ *   weights      [out, in] row-major fp32 (the .npy checkpoint layout)
+ *   statistics   softmax_m / softmax_l [B, T, H] fp32
+ * Device-pointer entry points run asynchronously on `stream` (a cudaStream_t,
+ * NULL = legacy default stream); *_host entry points take host buffers, copy
+ * them to the device, run, copy back and synchronise.
+ */
+#ifndef DIRKTENSOR_B200_H
+#define DIRKTENSOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ------------------------------------------------------------ */
+enum dt_status {
+    DT_OK = 0,
+    DT_ERR_INVALID_ARGUMENT = 1, /* bad shape, null or misaligned pointer        */
+    DT_ERR_CUDA = 2,             /* a CUDA runtime/driver call failed            */
+    DT_ERR_DEVICE_TIMEOUT = 3,   /* a kernel's bounded wait expired (no hang)    */
+    DT_ERR_UNSUPPORTED = 4,      /* e.g. head_dim != 128, no sm_100 device       */
+    DT_ERR_OUT_OF_MEMORY = 5,
+    DT_ERR_IO = 6                /* checkpoint file missing or malformed         */
+};
+
+/* Message for the last failing call on this thread ("" if none).
+ * Replaces the reference's exceptions (std::runtime_error, xt::load_npy throws;
+ * main.cpp:40, Detokenizer.cpp:44). */
+const char* dt_last_error(void);
+
+/* ABI version of this library (major * 10000 + minor * 100 + patch). */
+int dt_version(void);
+
+/* Synchronises the current device, then reports (and clears) a device-side
+ * error recorded by a kernel whose bounded wait expired: DT_ERR_DEVICE_TIMEOUT.
+ * The device-pointer entry points do not synchronise; call this after them. */
+int dt_check_device_error(void);
+
+/* ---- flash attention forward -------------------------------------------
+ * Replaces flash_attention_forward (FlashAttention.h:15-21,
+ * FlashAttention.cpp:24-182) and fills FlashAttentionResult
+ * (FlashAttention.h:6-10): o = softmax(scale * q k^T [+ causal mask]) v,
+ * softmax_m = row max of the scaled scores, softmax_l = sum exp(s - m).
+ * q, k, v, o: [B, T, H, D] fp32 device pointers; softmax_m/l may be NULL.
+ * D must be 128.  Operands are rounded to bf16 for the tensor cores
+ * (fp32 accumulation and softmax); the workspace holds those bf16 copies. */
+size_t dt_flash_fwd_workspace_bytes(int B, int T, int H, int D);
+int dt_flash_fwd(const float* q, const float* k, const float* v, float* o, float* softmax_m, float* softmax_l,
+                 int B, int T, int H, int D, float scale, int causal, void* workspace, size_t workspace_bytes,
+                 void* stream);
+/* Same with host buffers (the call the C++ drop-in flash_attention_forward makes). */
+int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, float* softmax_m,
+                      float* softmax_l, int B, int T, int H, int D, float scale, int causal);
+
+/* Packed-operand form used inside the layer and by head-sharded callers:
+ * q, k, v are bf16 [B, T, H, D] device arrays; o is fp32 (o_bf16 = 0) or
+ * bf16 (o_bf16 = 1) with o_row_stride elements between consecutive tokens
+ * (H*D for the dense layout).  seq_lens (device int[B], may be NULL) gives
+ * right-padded sequence lengths: rows t >= seq_lens[b] are written as zeros. */
+int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
+                      float* softmax_m, float* softmax_l, const int* seq_lens, int B, int T, int H, int D,
+                      float scale, int causal, void* stream);
+
+/* ---- attention layer ----------------------------------------------------
+ * Replaces class OlmoAttention (OlmoAttention.h:10-42): constructor
+ * (OlmoAttention.cpp:39-53) and forward (OlmoAttention.cpp:56-108):
+ *   y = (flash(rope(qnorm(x Wq^T)), rope(knorm(x Wk^T)), x Wv^T)) Wo^T
+ * with RMSNorm over all d_model columns (RMSNorm.cpp:15-22), rotate-half RoPE
+ * (OlmoAttention.cpp:18-36,111-146) and scale 1/sqrt(head_dim). */
+typedef struct dt_attn dt_attn;
+
+typedef struct dt_attn_weights {
+    const float* q_proj; /* [d_model, d_model] host fp32, [out, in] */
+    const float* k_proj;
+    const float* v_proj;
+    const float* o_proj;
+    const float* q_norm; /* [d_model] */
+    const float* k_norm;
+    int d_model;         /* 2048 (model_config.h:5) */
+    int n_heads;         /* 16   (model_config.h:6); head_dim must be 128 */
+    float eps;           /* RMSNorm eps, 1e-6 (RMSNorm.h:10) */
+    float rope_theta;    /* 500000 (OlmoAttention.cpp:16) */
+} dt_attn_weights;
+
+/* Uploads the weights (bf16 copies for the tensor cores) to `device`. */
+int dt_attn_create(const dt_attn_weights* w, int device, dt_attn** out);
+/* Reads {folder}/model.layers.{index}.self_attn.{q,k,v,o}_proj.weight.npy and
+ * {q,k}_norm.weight.npy (float32, C order), as OlmoAttention.cpp:39-46 does. */
+int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_attn** out);
+/* x, y: [B, T, d_model] fp32 device pointers.  seq_lens: device int[B] or
+ * NULL; with it, rows t >= seq_lens[b] of y are zero (right padding). */
+int dt_attn_forward(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y, void* stream);
+/* Same with host buffers; seq_lens is a host int[B] or NULL. */
+int dt_attn_forward_host(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y);
+int dt_attn_destroy(dt_attn* attn);
+
+/* ---- stages (for stage-wise parity checks and head-sharded callers) ----- */
+/* dst[i] = bf16(src[i]), n elements (n % 4 == 0). */
+int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream);
+/* C[M,N] = A[M,K] . B[N,K]^T; A, B bf16 row-major device; C fp32 (c_bf16 = 0)
+ * or bf16 (c_bf16 = 1) with ldc elements per row.  K % 8 == 0.
+ * The projection products of OlmoAttention.cpp:68,74,80,103-105. */
+int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, int N, int K, long long ldc,
+                    void* stream);
+/* Prologue: per token row r (position r % T), q/k RMSNorm over d_model = 2048
+ * with gains, rotate-half RoPE (head_dim 128), v copied; outputs bf16
+ * [B*T, 2048].  q, k, v: fp32 device rows with ld_in elements per row. */
+int dt_qk_norm_rope(const float* q, const float* k, const float* v, long long ld_in, const float* q_gain,
+                    const float* k_gain, void* q_out, void* k_out, void* v_out, int B, int T, float eps,
+                    float rope_theta, void* stream);
+/* Host copy of the RoPE tables the device uses ([max_seq, head_dim] each),
+ * computed like compute_rope_buffers (OlmoAttention.cpp:18-36). */
+int dt_rope_tables(float* sin_out, float* cos_out, int max_seq, int head_dim, float theta);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIRKTENSOR_B200_H */

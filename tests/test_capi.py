@@ -1,0 +1,74 @@
+"""CPU tests of the C ABI library: it loads, exports every symbol the header
+declares, validates arguments before touching a device, and its host-side RoPE
+tables equal the oracle's (compute_rope_buffers, OlmoAttention.cpp:18-36)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+import oracle
+from dirktensor_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dirktensor_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(dt_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(_lib.LIB_PATH)
+    syms = declared_symbols()
+    assert len(syms) >= 15
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, f"missing exports: {missing}"
+    # the Python binding covers the same set
+    assert set(syms) == set(_lib.SIGNATURES), set(syms) ^ set(_lib.SIGNATURES)
+
+
+def test_version_and_error_string():
+    L = _lib.lib()
+    assert L.dt_version() >= 100
+    assert isinstance(L.dt_last_error(), bytes)
+
+
+def test_argument_validation_without_device():
+    L = _lib.lib()
+    # head_dim 64 is rejected before any CUDA call
+    st = L.dt_flash_fwd(None, None, None, None, None, None, 1, 16, 2, 64, 0.1, 1, None, 0, None)
+    assert st == 4 and b"head_dim" in L.dt_last_error()
+    # K not a multiple of 8
+    st = L.dt_gemm_bf16_tn(None, None, None, 0, 16, 16, 12, 16, None)
+    assert st == 1 and b"K" in L.dt_last_error()
+    # cast count not a multiple of 4
+    st = L.dt_cast_f32_bf16(None, None, 6, None)
+    assert st == 1
+    # empty problems are a no-op success
+    assert L.dt_flash_fwd(None, None, None, None, None, None, 0, 16, 2, 128, 0.1, 1, None, 0, None) == 0
+    assert L.dt_gemm_bf16_tn(None, None, None, 0, 0, 16, 64, 16, None) == 0
+    # T beyond the RoPE table (model_config.h:4) is rejected
+    st = L.dt_qk_norm_rope(None, None, None, 6144, None, None, None, None, None, 1, 9000, 1e-6, 5e5, None)
+    assert st == 1 and b"max_seq_len" in L.dt_last_error()
+    assert L.dt_attn_forward(None, None, 1, 1, None, None, None) == 1
+    h = ctypes.c_void_p()
+    st = L.dt_attn_create_from_npy(b"/nonexistent-folder", 0, 0, ctypes.byref(h))
+    assert st == 6 and b"cannot open" in L.dt_last_error()
+
+
+def test_workspace_size():
+    L = _lib.lib()
+    n = 2 * 300 * 16 * 128
+    assert L.dt_flash_fwd_workspace_bytes(2, 300, 16, 128) >= 3 * n * 2
+    assert L.dt_flash_fwd_workspace_bytes(0, 300, 16, 128) == 0
+
+
+def test_rope_tables_equal_oracle():
+    import dirktensor_b200 as dt
+
+    s, c = dt.rope_tables(8192, 128, 500000.0)
+    os_, oc = oracle.rope_tables(8192, 128, 500000.0)
+    assert np.array_equal(s, os_) and np.array_equal(c, oc)
