@@ -1,0 +1,395 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+Workload (every N): configuration 4 -- head-parallel long-context attention,
+B=16, T=6144, H=16, D=128, Q/K/V fp32 N(0,1) (seeded synthetic data), causal,
+scale 1/sqrt(128), followed by the O projection (Wo 2048x2048, N(0, 0.02)).
+With N GPUs rank r owns heads [r*16/N, (r+1)*16/N); per-head outputs are
+exchanged token-sliced (NCCL all-to-all) and each rank projects B*T/N tokens.
+Total work is fixed, so scaling is "strong".
+
+A step = cast Q/K/V to bf16 -> flash attention -> exchange -> O projection.
+value      = (attention FLOPs 2*B*H*T^2*D + O-proj FLOPs 2*B*T*d^2) / step time,
+             device-resident inputs, CUDA events on the launching stream, max over ranks.
+e2e        = the same through host buffers: pinned Q/K/V slices copied in and the
+             y slice copied out inside the timed region.
+roofline   = the flash kernel (CUDA events around each launch in the timed region)
+             against the measured dense bf16 peak.
+cpu_baseline / --impl reference = the reference's own flash_attention_forward
+             (FlashAttention.cpp, compiled from the reference sources into
+             oracle/_ref) plus the O projection through OpenBLAS sgemm, on a bounded
+             sample of the same workload (whole batch elements), all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, T, H, D, DM = 16, 6144, 16, 128, 2048
+SCALE = 1.0 / np.sqrt(128.0)
+METRIC = "causal attn TFLOP/s + OLMo-2-1B prefill tok/s, T=512-6144, 1/2/4/8 B200"
+F_ATTN = 2.0 * B * H * T * T * D          # causal: 4*B*H*T^2*D / 2
+F_OPROJ = 2.0 * B * T * DM * DM
+PEAKS_FALLBACK = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return PEAKS_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", self.gpu_id], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                    power.append(float(parts[3]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        loaded = [s for s, p in zip(sm, power) if p > 300] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_id_for(torch, dev) -> str:
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[dev]
+        return str(dev)
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's own flash_attention_forward + OpenBLAS O projection
+# ---------------------------------------------------------------------------
+def reference_sample(n_batch: int, seed: int = 0):
+    """Runs the reference flash on n_batch whole batch elements (all 16 heads,
+    T=6144) and their O projection.  Returns (flops, seconds, threads, kind)."""
+    import oracle
+
+    ref = oracle.ref_lib()
+    kind = "reference"
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((n_batch, T, H, D), dtype=np.float32)
+    k = rng.standard_normal((n_batch, T, H, D), dtype=np.float32)
+    v = rng.standard_normal((n_batch, T, H, D), dtype=np.float32)
+    wo = (0.02 * rng.standard_normal((DM, DM), dtype=np.float32)).astype(np.float32)
+    threads = os.cpu_count() or 1
+    if ref is not None:
+        o, _, _, t_attn = oracle.ref_flash_fwd(q, k, v, SCALE, True, threads=0)
+        threads = ref.ref_get_threads()
+    else:  # the reference sources were not compiled: time the C restatement instead
+        kind = "port"
+        oracle.set_threads(0)
+        t0 = time.perf_counter()
+        o, _, _ = oracle.flash_fwd(q, k, v, SCALE, True)
+        t_attn = time.perf_counter() - t0
+    oracle.set_threads(0)
+    t0 = time.perf_counter()
+    oracle.linear(o.reshape(n_batch * T, DM), wo)
+    t_proj = time.perf_counter() - t0
+    flops = n_batch * (F_ATTN + F_OPROJ) / B
+    return flops, t_attn + t_proj, threads, kind
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    budget = 150.0  # seconds for the whole --warmup/--steps run
+    f1, t1, threads, kind = reference_sample(1, seed=1)  # calibration (counts as a warm-up)
+    per_step = budget / max(1, args.warmup + args.steps)
+    n_batch = int(max(1, min(B, per_step / max(t1, 1e-3))))
+    vals = []
+    for i in range(args.warmup + args.steps - 1):
+        f, t, threads, kind = reference_sample(n_batch, seed=2 + i)
+        if i >= args.warmup - 1:
+            vals.append((f, t))
+    if not vals:
+        vals = [(f1, t1)]
+    flops = sum(f for f, _ in vals)
+    secs = sum(t for _, t in vals)
+    value = flops / secs / 1e12
+    sample = f"{n_batch} of {B} batch elements x 16 heads, T={T}, per step"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": len(vals), "warmup": args.warmup, "ms_per_step": 1e3 * secs / len(vals), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4_head_parallel_attention", "B": B, "T": T, "H": H, "D": D,
+                   "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="dirktensor", choices=["dirktensor", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    import dirktensor_b200 as dt
+    from dirktensor_b200.head_parallel import HeadParallelAttention
+
+    Hl = H // world
+    M = B * T
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed * 1000 + rank)
+    q = torch.randn((B, T, Hl, D), generator=gen, device=dev)
+    k = torch.randn((B, T, Hl, D), generator=gen, device=dev)
+    v = torch.randn((B, T, Hl, D), generator=gen, device=dev)
+    gen.manual_seed(args.seed * 1000 + 999)
+    wo = torch.randn((DM, DM), generator=gen, device=dev) * 0.02
+    hp = HeadParallelAttention(wo, n_heads=H, head_dim=D)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident step -------------------------------------------
+    for _ in range(args.warmup):
+        hp.forward(q, k, v, SCALE, True)
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler(gpu_id_for(torch, local)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    fl_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record()
+    for i in range(args.steps):
+        hp.forward(q, k, v, SCALE, True, events=fl_events[i])
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    dt.check_device_error()
+    ms_step = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    ms_flash = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in fl_events))
+    flops_step = F_ATTN + F_OPROJ
+    value = flops_step / (ms_step * 1e-3) / 1e12
+
+    # ---- end to end through host buffers ----------------------------------
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    yh = torch.empty((M // world, DM), dtype=torch.float32).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        y = hp.forward(qd, kd, vd, SCALE, True)
+        yh.copy_(y, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e = {"value": flops_step / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
+           "h2d_bytes_per_step": 3 * q.numel() * 4 * world, "d2h_bytes_per_step": yh.numel() * 4 * world,
+           "api": "HeadParallelAttention.forward over the C ABI, pinned host buffers"}
+
+    # ---- config 1 at T=4096 (north-star single-GPU target) ---------------
+    t4096 = None
+    if world == 1:
+        t4096 = bench_t4096(torch, dt, dev, args)
+
+    # ---- CPU baseline (rank 0, N=1) ---------------------------------------
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        try:
+            f, s, threads, kind = reference_sample(1, seed=7)
+            cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+                   "sample": f"1 of {B} batch elements (16 heads, T={T}) attention + its O projection",
+                   "seconds": s}
+        except Exception as e:  # the oracle is optional at run time
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {e}"}
+
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    f_flash_rank = F_ATTN / world
+    achieved = f_flash_rank / (ms_flash * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "flash_fwd_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tj = json.load(f)
+            traffic = tj.get("bytes_per_launch_config4", {}).get(str(world))
+        except (OSError, ValueError):
+            traffic = None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config4_head_parallel_attention", "B": B, "T": T, "H": H, "D": D,
+                       "d_model": DM, "causal": True, "parallelism": f"head-parallel x{world} + token-sliced "
+                       "all-to-all + O-proj", "flops_per_step": flops_step,
+                       "l2": "inputs larger than L2 (805 MB fp32 per tensor in total)"},
+            "prefill_tok_s": M / (ms_step * 1e-3),
+            "roofline": {"bound": "tensor", "kernel": "flash_fwd_kernel", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": f"{src} bf16 burst",
+                         "ms_per_launch": ms_flash, "flops_per_launch": f_flash_rank, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 5 * args.steps,
+            "clocks": clocks,
+            "config1_t4096": t4096,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_t4096(torch, dt, dev, args):
+    """Config 1 at T=4096 (B=1, H=16): the single-GPU 50%-of-peak target.
+    Inputs are 32 MB per tensor (< L2), so L2 is flushed (256 MB write) before
+    every timed iteration, outside the events."""
+    Tt = 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(4096)
+    q, k, v = (torch.randn((1, Tt, H, D), generator=g, device=dev) for _ in range(3))
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    out = torch.empty((1, Tt, H, D), dtype=torch.float32, device=dev)
+    m = torch.empty((1, Tt, H), dtype=torch.float32, device=dev)
+    l = torch.empty_like(m)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.warmup + args.steps):
+        flush.fill_(float(i))
+        e = ev[i - args.warmup] if i >= args.warmup else None
+        if e:
+            e[0].record()
+        qb, kb, vb = dt.cast_bf16(q), dt.cast_bf16(k), dt.cast_bf16(v)
+        if e:
+            e[1].record()
+        dt.flash_attention_forward_bf16(qb, kb, vb, SCALE, True, out=out, softmax_m=m, softmax_l=l)
+        if e:
+            e[2].record()
+    torch.cuda.synchronize()
+    dt.check_device_error()
+    ms_cast = statistics.mean(a.elapsed_time(b) for a, b, _ in ev)
+    ms_flash = statistics.mean(b.elapsed_time(c) for _, b, c in ev)
+    f = 2.0 * H * Tt * Tt * D
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    return {"B": 1, "T": Tt, "H": H, "D": D, "flops": f, "ms_flash": ms_flash, "ms_cast": ms_cast,
+            "tflops_flash": f / (ms_flash * 1e-3) / 1e12, "frac_flash": f / (ms_flash * 1e-3) / 1e12 / peak,
+            "tflops_with_cast": f / ((ms_flash + ms_cast) * 1e-3) / 1e12, "peak": peak,
+            "peak_source": f"{src} bf16 burst", "l2": "flushed (256 MB write) before each iteration"}
+
+
+if __name__ == "__main__":
+    main()

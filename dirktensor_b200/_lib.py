@@ -71,6 +71,7 @@ SIGNATURES = {
     "dt_attn_destroy": (_I, [_P]),
     "dt_cast_f32_bf16": (_I, [_P, _P, _LL, _P]),
     "dt_gemm_bf16_tn": (_I, [_P, _P, _P, _I, _I, _I, _I, _LL, _P]),
+    "dt_gemm_bf16_tn_planar": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _LL, _P]),
     "dt_qk_norm_rope": (_I, [_P, _P, _P, _LL, _P, _P, _P, _P, _P, _I, _I, _F, _F, _P]),
     "dt_rope_tables": (_I, [_P, _P, _I, _I, _F]),
 }
@@ -83,7 +84,7 @@ def lib():
         if not os.path.exists(LIB_PATH):
             raise ImportError(
                 f"{LIB_PATH} not found: the CUDA library must be built first "
-                "(python -m dirktensor_b200.build); there is no CPU fallback")
+                "(python dirktensor_b200/build.py); there is no CPU fallback")
         L = ctypes.CDLL(LIB_PATH)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(L, name)

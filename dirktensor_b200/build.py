@@ -2,7 +2,7 @@
 
 The library is one translation unit (``csrc/capi.cu`` includes every kernel
 header), compiled by nvcc straight into the package directory so that the
-shared object travels with the source tree.  Run ``python -m dirktensor_b200.build``.
+shared object travels with the source tree.  Run ``python dirktensor_b200/build.py`` (by path: importing the package loads the library).
 """
 from __future__ import annotations
 

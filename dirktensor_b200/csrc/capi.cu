@@ -103,6 +103,22 @@ int make_map_2d(CUtensorMap* m, const void* base, long long rows, int K, int box
     return DT_OK;
 }
 
+// bf16 planar A: `planes` arrays [rows, plane_k] back to back -> 3-D map
+// (plane_k, rows, planes), box 64 x 128 x 1, 128 B swizzle.
+int make_map_planar(CUtensorMap* m, const void* base, long long rows, int plane_k, int planes) {
+    EncodeTiledFn enc;
+    DT_TRY(get_encode(&enc));
+    const cuuint64_t dims[3] = {(cuuint64_t)plane_k, (cuuint64_t)rows, (cuuint64_t)planes};
+    const cuuint64_t strides[2] = {(cuuint64_t)plane_k * 2, (cuuint64_t)rows * plane_k * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)dt::gemm::kBM, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled(planar) failed: %d", (int)r);
+    return DT_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Per-device state: kernel attributes, RoPE tables, host-API staging buffers
 // ---------------------------------------------------------------------------
@@ -272,10 +288,12 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
 }
 
 int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N, int K, long long ldc,
-                cudaStream_t st) {
+                cudaStream_t st, int a_planes = 1) {
     if (M == 0 || N == 0) return DT_OK;
     CUtensorMap ma, mb;
-    DT_TRY(make_map_2d(&ma, A, M, K, dt::gemm::kBM));
+    const int plane_k = K / a_planes;
+    if (a_planes > 1) DT_TRY(make_map_planar(&ma, A, M, plane_k, a_planes));
+    else DT_TRY(make_map_2d(&ma, A, M, K, dt::gemm::kBM));
     DT_TRY(make_map_2d(&mb, Bm, N, K, dt::gemm::kBN));
     dt::gemm::Params p;
     p.M = M;
@@ -284,6 +302,7 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     p.C = C;
     p.ldc = ldc;
     p.c_bf16 = c_bf16;
+    p.a_plane_k = a_planes > 1 ? plane_k : 0;
     dim3 grid((N + dt::gemm::kBN - 1) / dt::gemm::kBN, (M + dt::gemm::kBM - 1) / dt::gemm::kBM);
     dt::gemm::gemm_bf16_tn_kernel<<<grid, dt::gemm::kThreads, kGemmSmem, st>>>(ma, mb, p);
     DT_CUDA(cudaGetLastError());
@@ -475,6 +494,22 @@ int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, in
     int dev;
     DT_TRY(prepare_device(&dev));
     return launch_gemm(A, B, C, c_bf16 ? 1 : 0, M, N, K, ldc, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dt_gemm_bf16_tn_planar(const void* A, int a_planes, const void* B, void* C, int c_bf16, int M, int N, int K,
+                           long long ldc, void* stream) {
+    t_last_error.clear();
+    if (a_planes <= 0 || K <= 0 || (K % a_planes) != 0 || ((K / a_planes) % 64) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "K=%d must split into %d planes of a multiple of 64", K, a_planes);
+    if (M < 0 || N < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    if (M == 0 || N == 0) return DT_OK;
+    if (!A || !B || !C || !aligned16(A) || !aligned16(B) || !aligned16(C))
+        return fail(DT_ERR_INVALID_ARGUMENT, "A, B, C must be non-null and 16-byte aligned");
+    if (ldc < N || (ldc % (c_bf16 ? 8 : 4)) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ldc must be >= N and keep rows 16-byte aligned");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    return launch_gemm(A, B, C, c_bf16 ? 1 : 0, M, N, K, ldc, reinterpret_cast<cudaStream_t>(stream), a_planes);
 }
 
 int dt_qk_norm_rope(const float* q, const float* k, const float* v, long long ld_in, const float* q_gain,

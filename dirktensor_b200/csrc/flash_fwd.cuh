@@ -16,6 +16,7 @@
 //   warps 4-7  softmax warpgroup for Q1
 //   warp 8     TMA producer (Q0, Q1 once; then K0, V0, K1, V1, ... into a ring)
 //   warp 9     MMA issuer (one thread) and TMEM owner
+//   warps 10-11 idle (they complete warpgroup 2; registers are granted per warpgroup)
 // TMEM (512 columns x 128 lanes x 32 bit): S0 [0,128) S1 [128,256)
 // O0 [256,384) O1 [384,512); P_i (bf16 pairs) overwrites the first 64 columns
 // of S_i and feeds the PV product straight from TMEM.
@@ -40,7 +41,7 @@ constexpr int kQTiles = 2;
 constexpr int kStages = 4;
 constexpr int kTileBytes = kBM * kD * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2; // 128 rows x 128 B (one swizzle span of 64 bf16)
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // 3 warpgroups: registers are granted per warpgroup
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct Params {
@@ -95,7 +96,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int b, int t, int h
     }
 }
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -235,7 +236,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             mbar_wait(&sm.mma_done, 0, kSiteDone);
         }
         __syncwarp();
-    } else {
+    } else if (warp < 8) {
         // --------------------------- softmax warpgroups ---------------------
         const int i = warp >> 2;          // Q tile
         const int r = (warp & 3) * 32 + lane;
@@ -280,14 +281,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
                         alpha = ex2_approx(m_run - m_cand);
                         m_run = m_cand;
                     }
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        float o[32];
-                        tmem_ld32(tO + cc * 32, o);
+#pragma unroll 1
+                    for (int cc = 0; cc < 8; ++cc) {
+                        float o[16];
+                        tmem_ld16(tO + cc * 16, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                        tmem_st32(tO + cc * 32, o);
+                        for (int e = 0; e < 16; ++e) o[e] *= alpha;
+                        tmem_st16(tO + cc * 16, *reinterpret_cast<uint32_t(*)[16]>(o));
                     }
                 }
             }

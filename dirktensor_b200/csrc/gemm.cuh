@@ -12,6 +12,11 @@
 //   warp 0      TMA producer
 //   warp 1      MMA issuer (one thread) and TMEM owner
 //   warps 2-5   epilogue: TMEM -> registers -> global (one row per thread)
+// A may also be "planar": a_planes arrays [M, a_plane_k] stored back to back,
+// forming A[m, p*a_plane_k + x] = plane_p[m, x].  That is the layout in which
+// an all-to-all delivers a token slice of the per-head attention outputs from
+// head-sharded ranks (plane = source rank), so the O projection reads it with a
+// 3-D tensor map instead of a repacking pass.
 #pragma once
 #include "dt_common.cuh"
 
@@ -31,6 +36,7 @@ struct Params {
     void* C;            // [M, ldc] row-major
     long long ldc;      // elements
     int c_bf16;         // 0: fp32, 1: bf16
+    int a_plane_k;      // 0: A is [M, K]; else A is planar with planes of this K extent
 };
 
 struct __align__(1024) Smem {
@@ -86,7 +92,12 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                 const uint32_t ph = (kb / kStages) & 1;
                 if (!mbar_wait(&sm.empty[s], ph ^ 1, kSiteEmpty)) break;
                 mbar_arrive_expect_tx(&sm.full[s], kABytes + kBBytes);
-                tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK, m0);
+                if (p.a_plane_k) {
+                    const int plane = (kb * kBK) / p.a_plane_k;
+                    tma_load_3d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK - plane * p.a_plane_k, m0, plane);
+                } else {
+                    tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK, m0);
+                }
                 tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * kBK, n0);
                 ++issued;
             }

@@ -115,6 +115,13 @@ int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream);
  * The projection products of OlmoAttention.cpp:68,74,80,103-105. */
 int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, int N, int K, long long ldc,
                     void* stream);
+/* The same product with a planar A: a_planes arrays [M, K/a_planes] stored
+ * back to back (A[m, p*(K/a_planes) + x] = plane_p[m, x]); K/a_planes must be a
+ * multiple of 64.  This is the O projection (OlmoAttention.cpp:103-105) of the
+ * head-parallel path: after the all-to-all, plane p holds source rank p's heads
+ * for this rank's token slice. */
+int dt_gemm_bf16_tn_planar(const void* A, int a_planes, const void* B, void* C, int c_bf16, int M, int N, int K,
+                           long long ldc, void* stream);
 /* Prologue: per token row r (position r % T), q/k RMSNorm over d_model = 2048
  * with gains, rotate-half RoPE (head_dim 128), v copied; outputs bf16
  * [B*T, 2048].  q, k, v: fp32 device rows with ld_in elements per row. */

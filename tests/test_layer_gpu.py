@@ -19,7 +19,9 @@ def test_gemm_vs_torch_fp32(cuda, M, N, K):
     a = torch.from_numpy(randn(M + N, (M, K))).to(cuda).to(torch.bfloat16)
     b = torch.from_numpy(randn(K + 1, (N, K), 0.05)).to(cuda).to(torch.bfloat16)
     c = dt.gemm_bf16_tn(a, b)
-    cb = dt.gemm_bf16_tn(a, b, out_bf16=True)
+    # bf16 rows must stay 16-byte aligned: pad the leading dimension to a multiple of 8
+    cb = dt.gemm_bf16_tn(a, b, out=torch.empty((M, (N + 7) // 8 * 8), dtype=torch.bfloat16, device=cuda),
+                         out_bf16=True)[:, :N]
     dt.check_device_error()
     ref = a.float() @ b.float().t()
     assert rel_l2(c.cpu().numpy(), ref.cpu().numpy()) < TOL_GEMM_REL_L2
