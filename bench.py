@@ -200,12 +200,18 @@ def main():
     ap.add_argument("--impl", default="dirktensor", choices=["dirktensor", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, choices=["flash_bf16", "layer"],
+                    help="profiling case for ncu: a few launches of one stage, no timing")
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--seq", type=int, default=4096)
     args = ap.parse_args()
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
     local = env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.case:
+        return run_case(args)
     if args.warmup < 3:
         args.warmup = 3
 
@@ -306,9 +312,11 @@ def main():
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         try:
-            f, s, threads, kind = reference_sample(1, seed=7)
+            f1, s1, _, _ = reference_sample(1, seed=7)  # calibration: size the sample to ~10 s
+            nb = int(max(1, min(B, 10.0 / max(s1, 1e-3))))
+            f, s, threads, kind = reference_sample(nb, seed=8)
             cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-                   "sample": f"1 of {B} batch elements (16 heads, T={T}) attention + its O projection",
+                   "sample": f"{nb} of {B} batch elements (16 heads, T={T}) attention + their O projection",
                    "seconds": s}
         except Exception as e:  # the oracle is optional at run time
             cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "reference",
@@ -389,6 +397,34 @@ def bench_t4096(torch, dt, dev, args):
             "tflops_flash": f / (ms_flash * 1e-3) / 1e12, "frac_flash": f / (ms_flash * 1e-3) / 1e12 / peak,
             "tflops_with_cast": f / ((ms_flash + ms_cast) * 1e-3) / 1e12, "peak": peak,
             "peak_source": f"{src} bf16 burst", "l2": "flushed (256 MB write) before each iteration"}
+
+
+def run_case(args):
+    """Small fixed workloads for ncu captures (one GPU, a few launches)."""
+    import torch
+
+    import dirktensor_b200 as dt
+
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    Bc, Tc = args.batch, args.seq
+    if args.case == "flash_bf16":
+        q, k, v = (torch.randn((Bc, Tc, H, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+        out = torch.empty((Bc, Tc, H, D), device=dev)
+        for _ in range(3):
+            dt.flash_attention_forward_bf16(q, k, v, SCALE, True, out=out)
+    else:
+        rng = np.random.default_rng(0)
+        w = [0.02 * rng.standard_normal((DM, DM), dtype=np.float32) for _ in range(4)]
+        gains = [np.ones(DM, np.float32), np.ones(DM, np.float32)]
+        attn = dt.OlmoAttention.from_weights(*w, *gains)
+        x = torch.randn((Bc, Tc, DM), generator=g, device=dev)
+        for _ in range(3):
+            attn.forward(x)
+    torch.cuda.synchronize()
+    dt.check_device_error()
+    print("ok", args.case, Bc, Tc)
 
 
 if __name__ == "__main__":

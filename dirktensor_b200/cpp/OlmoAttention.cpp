@@ -1,0 +1,57 @@
+// OlmoAttention over the C ABI (dt_attn_create_from_npy / dt_attn_forward_host).
+#include "OlmoAttention.h"
+
+#include <cstdlib>
+#include <stdexcept>
+#include <string>
+#include <utility>
+
+#include "dirktensor_b200.h"
+#include "model_config.h"
+
+namespace {
+int device_from_env() {
+    const char* s = std::getenv("DIRKTENSOR_B200_DEVICE");
+    return s ? std::atoi(s) : 0;
+}
+[[noreturn]] void raise(const char* what) { throw std::runtime_error(std::string(what) + ": " + dt_last_error()); }
+}  // namespace
+
+OlmoAttention::OlmoAttention(const std::string& folder, unsigned int index) {
+    if (dt_attn_create_from_npy(folder.c_str(), index, device_from_env(), &m_handle) != DT_OK)
+        raise("OlmoAttention");
+}
+
+OlmoAttention::~OlmoAttention() {
+    if (m_handle) dt_attn_destroy(m_handle);
+}
+
+OlmoAttention::OlmoAttention(OlmoAttention&& other) noexcept : m_handle(std::exchange(other.m_handle, nullptr)) {}
+
+OlmoAttention& OlmoAttention::operator=(OlmoAttention&& other) noexcept {
+    if (this != &other) {
+        if (m_handle) dt_attn_destroy(m_handle);
+        m_handle = std::exchange(other.m_handle, nullptr);
+    }
+    return *this;
+}
+
+xt::xtensor<float, 3> OlmoAttention::forward(const xt::xtensor<float, 3>& input) {
+    const std::size_t b = input.shape(0), t = input.shape(1), d = input.shape(2);
+    if (d != d_model) throw std::invalid_argument("OlmoAttention::forward: last dimension must be d_model");
+    xt::xtensor<float, 3> out = xt::empty<float>({b, t, d});
+    if (dt_attn_forward_host(m_handle, input.data(), static_cast<int>(b), static_cast<int>(t), nullptr,
+                             out.data()) != DT_OK)
+        raise("OlmoAttention::forward");
+    return out;
+}
+
+xt::xtensor<float, 3> OlmoAttention::backward(const xt::xtensor<float, 3>&) {
+    throw std::logic_error("OlmoAttention::backward: the B200 drop-in implements the forward path only");
+}
+
+void OlmoAttention::step(float) {
+    throw std::logic_error("OlmoAttention::step: the B200 drop-in implements the forward path only");
+}
+
+void OlmoAttention::zero_grad() {}

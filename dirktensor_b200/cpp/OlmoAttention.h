@@ -1,0 +1,35 @@
+// Drop-in for the reference's OlmoAttention (OlmoAttention.h:10-42): the same
+// public interface, so OlmoBlock (which holds it by value, OlmoBlock.h:19, and
+// calls forward/backward/step/zero_grad, OlmoBlock.cpp:6-40) compiles
+// unchanged.  The weights live on the GPU (bf16 projections, fp32 norm gains)
+// behind an opaque handle of the C ABI; the class is therefore move-only.
+#pragma once
+
+#include <string>
+#include <xtensor/containers/xtensor.hpp>
+
+struct dt_attn;
+
+class OlmoAttention {
+public:
+    // Loads {folder}/model.layers.{index}.self_attn.{q,k,v,o}_proj.weight.npy and
+    // {q,k}_norm.weight.npy (OlmoAttention.cpp:39-46).  The GPU is taken from
+    // the DIRKTENSOR_B200_DEVICE environment variable (default 0).
+    OlmoAttention(const std::string& folder, unsigned int index);
+    ~OlmoAttention();
+    OlmoAttention(OlmoAttention&& other) noexcept;
+    OlmoAttention& operator=(OlmoAttention&& other) noexcept;
+    OlmoAttention(const OlmoAttention&) = delete;
+    OlmoAttention& operator=(const OlmoAttention&) = delete;
+
+    // input (batch, seq, d_model) -> (batch, seq, d_model)  (OlmoAttention.cpp:56-108)
+    xt::xtensor<float, 3> forward(const xt::xtensor<float, 3>& input);
+    // Training path (OlmoAttention.cpp:149-330): not provided; throws std::logic_error.
+    xt::xtensor<float, 3> backward(const xt::xtensor<float, 3>& d_output);
+    void step(float lr);
+    // No gradients are held on the forward-only path: nothing to clear.
+    void zero_grad();
+
+private:
+    dt_attn* m_handle = nullptr;
+};

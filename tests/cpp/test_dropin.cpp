@@ -1,0 +1,77 @@
+// Exercises the C++ drop-in the way the reference's code calls it:
+// flash_attention_forward(Q, K, V, scale, true) (OlmoAttention.cpp:94) and an
+// OlmoBlock-like owner holding OlmoAttention by value (OlmoBlock.h:19) that
+// constructs it from (folder, index) and calls forward (OlmoBlock.cpp:6,14).
+//
+//   test_dropin flash <dir> B T H     reads dir/{q,k,v}.f32, writes dir/{o,m,l}.f32
+//   test_dropin layer <dir> index B T reads dir/x.f32 and the layer's .npy weights
+//                                     from dir, writes dir/y.f32
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <iostream>
+#include <stdexcept>
+#include <string>
+
+#include "FlashAttention.h"
+#include "OlmoAttention.h"
+
+template <class X>
+static void read_into(const std::string& path, X& x) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) throw std::runtime_error("cannot open " + path);
+    f.read(reinterpret_cast<char*>(x.data()), static_cast<std::streamsize>(x.size() * sizeof(float)));
+}
+
+template <class X>
+static void write_from(const std::string& path, const X& x) {
+    std::ofstream f(path, std::ios::binary);
+    f.write(reinterpret_cast<const char*>(x.data()), static_cast<std::streamsize>(x.size() * sizeof(float)));
+}
+
+struct BlockLike {
+    OlmoAttention m_attention;
+    BlockLike(const std::string& folder, unsigned index) : m_attention(folder, index) {}
+    xt::xtensor<float, 3> forward(const xt::xtensor<float, 3>& x) { return m_attention.forward(x); }
+};
+
+int main(int argc, char** argv) {
+    try {
+        if (argc < 3) throw std::runtime_error("usage: test_dropin flash|layer <dir> ...");
+        const std::string mode = argv[1], dir = argv[2];
+        if (mode == "flash" && argc == 6) {
+            const std::size_t B = std::stoul(argv[3]), T = std::stoul(argv[4]), H = std::stoul(argv[5]);
+            xt::xtensor<float, 4> q = xt::empty<float>({B, T, H, std::size_t(128)});
+            xt::xtensor<float, 4> k = xt::empty<float>({B, T, H, std::size_t(128)});
+            xt::xtensor<float, 4> v = xt::empty<float>({B, T, H, std::size_t(128)});
+            read_into(dir + "/q.f32", q);
+            read_into(dir + "/k.f32", k);
+            read_into(dir + "/v.f32", v);
+            const FlashAttentionResult r = flash_attention_forward(q, k, v, 1.0f / 11.313708498984761f, true);
+            write_from(dir + "/o.f32", r.output);
+            write_from(dir + "/m.f32", r.softmax_m);
+            write_from(dir + "/l.f32", r.softmax_l);
+            try {
+                flash_attention_backward(r.output, r.output, r.softmax_m, r.softmax_l, q, k, v, 0.1f);
+                return 3;  // must not succeed
+            } catch (const std::logic_error&) {
+            }
+        } else if (mode == "layer" && argc == 6) {
+            const unsigned index = static_cast<unsigned>(std::stoul(argv[3]));
+            const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);
+            xt::xtensor<float, 3> x = xt::empty<float>({B, T, std::size_t(2048)});
+            read_into(dir + "/x.f32", x);
+            BlockLike block(dir, index);
+            BlockLike moved(std::move(block));  // the class is move-only
+            const xt::xtensor<float, 3> y = moved.forward(x);
+            write_from(dir + "/y.f32", y);
+            moved.m_attention.zero_grad();
+        } else {
+            throw std::runtime_error("bad arguments");
+        }
+    } catch (const std::exception& e) {
+        std::cerr << "error: " << e.what() << "\n";
+        return 1;
+    }
+    return 0;
+}
