@@ -455,6 +455,76 @@ int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, 
     return read_device_error(&had);
 }
 
+// ---- flash attention forward without any allocation ------------------------
+//
+// For callers that must not allocate device memory themselves or have the
+// library do it: a serving engine that reserves its whole HBM budget up front
+// and hands out every byte through its own pool, a plugin running inside a
+// host framework that forbids allocation from its callbacks, or a latency
+// critical loop where cudaMalloc/cudaFree (which can synchronise the device)
+// are not acceptable.  dt_flash_fwd needs a workspace for the bf16 copies of
+// Q, K and V; this variant keeps that workspace in a fixed array that is part
+// of the library's device image, so a call allocates nothing.
+//
+// Limits and behaviour:
+//  * The array is kNoAllocScratchBytes (24 MiB) on every GPU that loads the
+//    library, held until the process exits.  It fits B*T*H*D <= 4,194,304
+//    elements (for example B=1, T=2048, H=16, D=128); larger problems are
+//    rejected with DT_ERR_INVALID_ARGUMENT before anything is launched.
+//  * All calls on a device share the one array, and it keeps whatever the last
+//    call wrote.  Nothing in it has to start at zero (each call overwrites the
+//    part it reads), so it is never cleared.  Calls whose kernels can overlap
+//    on the GPU (different streams, no ordering between them) race on it; order
+//    them on one stream or with events.
+//  * The first call on a device, with that device current, looks up the
+//    array's device address (cudaGetSymbolAddress) and caches it.  Make that
+//    first call before any stream capture.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[24u << 20];
+constexpr size_t kNoAllocScratchBytes = sizeof(g_noalloc_scratch);
+
+namespace {
+void* g_noalloc_addr[64] = {};
+
+int noalloc_scratch(int dev, void** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr)
+            return fail(DT_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed: %s", cudaGetErrorString(e));
+        g_noalloc_addr[dev] = ptr;
+    }
+    *out = g_noalloc_addr[dev];
+    return DT_OK;
+}
+}  // namespace
+
+int dt_flash_fwd_noalloc(const float* q, const float* k, const float* v, float* o, float* softmax_m,
+                         float* softmax_l, int B, int T, int H, int D, float scale, int causal, void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (!q || !k || !v || !o) return fail(DT_ERR_INVALID_ARGUMENT, "null q/k/v/o");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v/o must be 16-byte aligned");
+    const long long n = (long long)B * T * H * D;
+    const size_t one = align256((size_t)n * 2);
+    if (3 * one > kNoAllocScratchBytes)
+        return fail(DT_ERR_INVALID_ARGUMENT,
+                    "dt_flash_fwd_noalloc: B*T*H*D = %lld exceeds the fixed scratch (at most %zu elements); "
+                    "use dt_flash_fwd with a caller workspace",
+                    n, kNoAllocScratchBytes / 6);
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    void* scratch;
+    DT_TRY(noalloc_scratch(dev, &scratch));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t* ws = reinterpret_cast<uint8_t*>(scratch);
+    DT_TRY(launch_cast3(q, k, v, ws, ws + one, ws + 2 * one, n, st));
+    return launch_flash(ws, ws + one, ws + 2 * one, o, 0, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H,
+                        scale, causal, st);
+}
+
 int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
                       float* softmax_m, float* softmax_l, const int* seq_lens, int B, int T, int H, int D,
                       float scale, int causal, void* stream) {

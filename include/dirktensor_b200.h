@@ -65,6 +65,19 @@ int dt_flash_fwd(const float* q, const float* k, const float* v, float* o, float
 int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, float* softmax_m,
                       float* softmax_l, int B, int T, int H, int D, float scale, int causal);
 
+/* Same as dt_flash_fwd, but allocates nothing and takes no workspace: the
+ * bf16 operand copies live in a fixed 24 MiB array inside the library's device
+ * image (present on every GPU that loads the library until exit).  No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory (an engine that owns its whole HBM budget through its own
+ * pool, a plugin barred from allocating in callbacks, a loop that cannot
+ * afford cudaMalloc's synchronisation).  B*T*H*D must be <= 4,194,304, else
+ * DT_ERR_INVALID_ARGUMENT.  All calls share the array: calls that may overlap
+ * on the GPU race and must be ordered by the caller.  The first call on a
+ * device looks up the array's address; make it before any stream capture. */
+int dt_flash_fwd_noalloc(const float* q, const float* k, const float* v, float* o, float* softmax_m,
+                         float* softmax_l, int B, int T, int H, int D, float scale, int causal, void* stream);
+
 /* Packed-operand form used inside the layer and by head-sharded callers:
  * q, k, v are bf16 [B, T, H, D] device arrays; o is fp32 (o_bf16 = 0) or
  * bf16 (o_bf16 = 1) with o_row_stride elements between consecutive tokens
