@@ -202,6 +202,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, choices=["flash_bf16", "layer"],
                     help="profiling case for ncu: a few launches of one stage, no timing")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config-1 sweep (T = 64 ... 6144) and config 4: flash kernel TFLOP/s per shape")
     ap.add_argument("--batch", type=int, default=4)
     ap.add_argument("--seq", type=int, default=4096)
     args = ap.parse_args()
@@ -212,6 +214,8 @@ def main():
         return run_reference(args, rank)
     if args.case:
         return run_case(args)
+    if args.sweep:
+        return run_sweep(args)
     if args.warmup < 3:
         args.warmup = 3
 
@@ -308,6 +312,10 @@ def main():
     if world == 1:
         t4096 = bench_t4096(torch, dt, dev, args)
 
+    layers = None
+    if world == 1:
+        layers = bench_layers(torch, dt, dev, args)
+
     # ---- CPU baseline (rank 0, N=1) ---------------------------------------
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -354,11 +362,52 @@ def main():
             "gpu_launches": 5 * args.steps,
             "clocks": clocks,
             "config1_t4096": t4096,
+            "layers": layers,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def bench_layers(torch, dt, dev, args):
+    """One OLMo-2-1B attention layer (OlmoAttention::forward) on the device:
+    config 0 (B=1, T=512) and config 2 (B=8, T_max=2048, right-padded, seeded
+    lengths in [256, 2048]).  tok/s counts valid tokens; FLOPs = projections
+    2*tokens*2048*8192 + causal attention 2*H*len^2*D per sequence.  L2 is
+    flushed before every timed forward."""
+    rng = np.random.default_rng(0)
+    w = [(0.02 * rng.standard_normal((DM, DM), dtype=np.float32)) for _ in range(4)]
+    gains = [(1 + 0.02 * rng.standard_normal(DM, dtype=np.float32)).astype(np.float32) for _ in range(2)]
+    attn = dt.OlmoAttention.from_weights(*w, *gains, device=dev.index or 0)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    out = {}
+    for name, Bl, Tl, lens in [("config0", 1, 512, None),
+                               ("config2", 8, 2048, np.random.default_rng(2).integers(256, 2049, 8))]:
+        x = torch.from_numpy(rng.standard_normal((Bl, Tl, DM), dtype=np.float32)).to(dev)
+        y = torch.empty_like(x)
+        lens_t = None if lens is None else torch.as_tensor(lens, dtype=torch.int32, device=dev)
+        valid = Bl * Tl if lens is None else int(np.sum(lens))
+        seqs = [Tl] * Bl if lens is None else [int(v) for v in lens]
+        flops = 2.0 * valid * DM * 8192 + sum(2.0 * H * L * L * D for L in seqs)
+        reps = max(3, min(args.steps, 20))
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            torch.cuda._sleep(2_000_000)
+            e = ev[i - args.warmup] if i >= args.warmup else None
+            if e:
+                e[0].record()
+            attn.forward(x, seq_lens=lens_t, out=y)
+            if e:
+                e[1].record()
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+        out[name] = {"B": Bl, "T": Tl, "valid_tokens": valid, "ms": ms, "tok_s": valid / (ms * 1e-3),
+                     "tflops": flops / (ms * 1e-3) / 1e12}
+    dt.check_device_error()
+    attn.close()
+    return out
 
 
 def bench_t4096(torch, dt, dev, args):
@@ -397,6 +446,54 @@ def bench_t4096(torch, dt, dev, args):
             "tflops_flash": f / (ms_flash * 1e-3) / 1e12, "frac_flash": f / (ms_flash * 1e-3) / 1e12 / peak,
             "tflops_with_cast": f / ((ms_flash + ms_cast) * 1e-3) / 1e12, "peak": peak,
             "peak_source": f"{src} bf16 burst", "l2": "flushed (256 MB write) before each iteration"}
+
+
+def run_sweep(args):
+    """Flash kernel alone (bf16 operands already in HBM) and with the fp32->bf16
+    casts, for config 1 (B=1, H=16, T = 64 ... 6144) and config 4 (B=16, T=6144).
+    L2 is flushed (256 MB write) before every timed launch, outside the events,
+    and a GPU-side spin before the start event hides the host's launch latency."""
+    import torch
+
+    import dirktensor_b200 as dt
+
+    dev = torch.device("cuda:0")
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    rows = []
+    for Bs, Ts in [(1, 64), (1, 512), (1, 1024), (1, 2048), (1, 4096), (1, 6144), (16, 6144)]:
+        q, k, v = (torch.randn((Bs, Ts, H, D), generator=g, device=dev) for _ in range(3))
+        out = torch.empty_like(q)
+        reps = max(3, min(args.steps, 20))
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps)]
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            # keep the GPU busy while the host queues the launches below, so the
+            # events time the kernels and not the host's launch latency
+            torch.cuda._sleep(2_000_000)
+            e = ev[i - args.warmup] if i >= args.warmup else None
+            if e:
+                e[0].record()
+            qb, kb, vb = dt.cast_bf16(q), dt.cast_bf16(k), dt.cast_bf16(v)
+            if e:
+                e[1].record()
+            dt.flash_attention_forward_bf16(qb, kb, vb, SCALE, True, out=out)
+            if e:
+                e[2].record()
+        torch.cuda.synchronize()
+        ms_flash = statistics.median(a.elapsed_time(b) for _, a, b in ev)
+        ms_cast = statistics.median(a.elapsed_time(b) for a, b, _ in ev)
+        f = 2.0 * Bs * H * Ts * Ts * D
+        rows.append({"B": Bs, "T": Ts, "ms_flash": ms_flash, "tflops_flash": f / ms_flash / 1e9,
+                     "frac_flash": f / ms_flash / 1e9 / peak, "ms_cast": ms_cast,
+                     "tflops_with_cast": f / (ms_flash + ms_cast) / 1e9})
+        del q, k, v, out, qb, kb, vb
+    dt.check_device_error()
+    print(json.dumps({"sweep": "flash_fwd causal, H=16, D=128", "peak": peak, "peak_source": f"{src} bf16 burst",
+                      "rows": rows}), flush=True)
 
 
 def run_case(args):

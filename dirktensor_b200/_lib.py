@@ -10,7 +10,8 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libdirktensor_b200.so")
+# DIRKTENSOR_B200_LIB may point at another build of the same library.
+LIB_PATH = os.environ.get("DIRKTENSOR_B200_LIB") or os.path.join(HERE, "libdirktensor_b200.so")
 
 DT_OK = 0
 STATUS_NAMES = {

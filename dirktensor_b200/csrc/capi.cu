@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -124,6 +125,7 @@ int make_map_planar(CUtensorMap* m, const void* base, long long rows, int plane_
 // ---------------------------------------------------------------------------
 struct DevState {
     bool attrs = false;
+    int num_sms = 148;
     float* sin_t = nullptr;
     float* cos_t = nullptr;
     float rope_theta = 0.f;
@@ -152,6 +154,7 @@ int ensure_attrs(int dev) {
     if (prop.major != 10)
         return fail(DT_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
                     prop.major, prop.minor);
+    s.num_sms = prop.multiProcessorCount;
     DT_CUDA(cudaFuncSetAttribute(dt::flash::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kFlashSmem));
     DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -271,6 +274,25 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     p.T = T;
     p.H = H;
     p.nblk = (T + 255) / 256;
+    {
+        // Scheduling groups of (b, h) pairs.  When the K/V of all heads fit in L2
+        // (<= 64 MB of bf16) one group keeps a global heaviest-first order.
+        // Otherwise each group holds about two waves of blocks -- enough to fill
+        // the GPU, few enough heads that their K/V stay in L2 -- and the groups
+        // are sized evenly so the last one is not a short tail.
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
+        const int BH = B * H;
+        const double kv_bytes = (double)BH * T * 128 * 2 * 2;
+        if (kv_bytes <= 64.0 * 1024 * 1024) {
+            p.group = BH;
+        } else {
+            const int want = std::max(1, (2 * sms + p.nblk - 1) / p.nblk);
+            const int ngroups = (BH + want - 1) / want;
+            p.group = (BH + ngroups - 1) / ngroups;
+        }
+    }
     p.causal = causal ? 1 : 0;
     p.scale = scale;
     p.scale_log2 = scale * 1.4426950408889634f;
@@ -303,7 +325,14 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     p.ldc = ldc;
     p.c_bf16 = c_bf16;
     p.a_plane_k = a_planes > 1 ? plane_k : 0;
-    dim3 grid((N + dt::gemm::kBN - 1) / dt::gemm::kBN, (M + dt::gemm::kBM - 1) / dt::gemm::kBM);
+    p.tiles_n = (N + dt::gemm::kBN - 1) / dt::gemm::kBN;
+    const long long tiles = (long long)p.tiles_n * ((M + dt::gemm::kBM - 1) / dt::gemm::kBM);
+    if (tiles > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "GEMM too large");
+    p.num_tiles = (int)tiles;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
+    const int grid = (int)std::min<long long>(tiles, sms);  // persistent: one CTA per SM
     dt::gemm::gemm_bf16_tn_kernel<<<grid, dt::gemm::kThreads, kGemmSmem, st>>>(ma, mb, p);
     DT_CUDA(cudaGetLastError());
     return DT_OK;

@@ -97,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no cluster multicast anywhere in this code base)
+// TMA tile loads (each CTA loads its own tiles from this GPU's memory)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -248,6 +248,54 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+
+// Packed fp32 pair helpers (sm_100 f32x2 FMA/ADD: one instruction for two lanes of work).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x for two values on the FMA pipe instead of the MUFU (exp) unit.
+// x = n + f with n = rint(x), taken from the low mantissa bits of x + 1.5*2^23
+// (exact for |x| < 2^22); 2^f on [-1/2, 1/2] is a degree-3 polynomial whose
+// coefficients were fitted for this code by weighted least squares on
+// Chebyshev nodes (relative error <= 7.5e-5 in fp32 Horner form, far below the
+// bf16 rounding applied to the result); n is then added to the exponent field.
+// Inputs are clamped to >= -125 so the exponent cannot underflow; callers use
+// this only on unmasked scores (no -inf).
+__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
+    const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+    const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
+    const uint64_t r = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+    const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), x);
+    uint64_t p = f2_fma(f2_pack(0.055171624f, 0.055171624f), f, f2_pack(0.24261113f, 0.24261113f));
+    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+    float p0, p1, t0, t1;
+    f2_unpack(p, p0, p1);
+    f2_unpack(t, t0, t1);
+    y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+    y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

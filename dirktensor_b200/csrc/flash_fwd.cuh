@@ -43,10 +43,20 @@ constexpr int kTileBytes = kBM * kD * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2; // 128 rows x 128 B (one swizzle span of 64 bf16)
 constexpr int kThreads = 384;  // 3 warpgroups: registers are granted per warpgroup
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Of every 16 column pairs of an unmasked S tile, this many compute 2^x on the
+// FMA pipe (exp2_poly_pair) instead of the MUFU.  Measured on B200 with 0, 2, 4
+// and 6 pairs: every step away from 0 was slower at every shape (the softmax is
+// bound by its instruction stream and latency chain, not by the MUFU rate), so
+// the default is 0; the path stays available for a schedule that is MUFU-bound.
+#ifndef DT_FLASH_EMU_PAIRS
+#define DT_FLASH_EMU_PAIRS 0
+#endif
+constexpr int kEmuPairs = DT_FLASH_EMU_PAIRS;
 
 struct Params {
     int B, T, H;
     int nblk;               // 256-row blocks per (b, h)
+    int group;              // (b, h) pairs per scheduling group (L2-resident K/V working set)
     int causal;
     float scale;            // the caller's scale (reference: 1/sqrt(head_dim))
     float scale_log2;       // scale * log2(e)
@@ -105,10 +115,18 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // ---- work item: heaviest 256-row blocks first -------------------------
+    // ---- work item ------------------------------------------------------
+    // (b, h) pairs are taken in groups of p.group; inside a group the blocks run
+    // heaviest (highest c) first.  CTAs are dispatched in blockIdx order, so the
+    // K/V of one group (group * T * 512 B) stay in L2 while its blocks run.
     const int BH = p.B * p.H;
-    const int c = p.nblk - 1 - static_cast<int>(blockIdx.x) / BH;
-    const int bh = static_cast<int>(blockIdx.x) % BH;
+    const int per_group = p.group * p.nblk;
+    const int gi = static_cast<int>(blockIdx.x) / per_group;
+    const int g0 = gi * p.group;
+    const int gsz = min(p.group, BH - g0);
+    const int gidx = static_cast<int>(blockIdx.x) - gi * per_group;
+    const int c = p.nblk - 1 - gidx / gsz;
+    const int bh = g0 + gidx % gsz;
     const int b = bh / p.H;
     const int h = bh % p.H;
     const int Tb = p.seq_lens ? min(max(p.seq_lens[b], 0), p.T) : p.T;
@@ -266,9 +284,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
                 for (int e = 0; e < 128; ++e)
                     if (k0 + e > lim) s[e] = -INFINITY;
             }
-            float rmax = s[0];
+            // Row max as 8 independent chains over 16-column slices, then a short
+            // combine: a single 64-deep chain of dependent max ops is latency-bound.
+            float pm[8];
 #pragma unroll
-            for (int e = 1; e < 128; ++e) rmax = fmaxf(rmax, s[e]);
+            for (int g = 0; g < 8; ++g) {
+                float a = fmax3(s[16 * g], s[16 * g + 1], s[16 * g + 2]);
+#pragma unroll
+                for (int e = 3; e < 15; e += 2) a = fmax3(a, s[16 * g + e], s[16 * g + e + 1]);
+                pm[g] = fmaxf(a, s[16 * g + 15]);
+            }
+            const float rmax = fmaxf(fmax3(pm[0], pm[1], pm[2]), fmax3(fmax3(pm[3], pm[4], pm[5]), pm[6], pm[7]));
             mx = fmaxf(mx, rmax);
             const float m_cand = rmax * p.scale_log2;
             float alpha = 1.f;
@@ -292,20 +318,34 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
                     }
                 }
             }
-            const float neg_m = -m_run;
-            float sum = 0.f;
+            // p = 2^(s*scale*log2e - m): the scale-subtract and the row sum run as
+            // packed f32x2 pairs; ex2 stays per element (MUFU).
+            const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
+            const uint64_t nm2 = f2_pack(-m_run, -m_run);
+            // one packed partial sum per 32-column chunk: four independent chains
+            uint64_t sum2[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+            const bool masked = diag || tail;
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const float p0 = ex2_approx(fmaf(s[cc * 32 + 2 * e], p.scale_log2, neg_m));
-                    const float p1 = ex2_approx(fmaf(s[cc * 32 + 2 * e + 1], p.scale_log2, neg_m));
-                    sum += p0 + p1;
+                    float x0, x1, p0, p1;
+                    f2_unpack(f2_fma(f2_pack(s[cc * 32 + 2 * e], s[cc * 32 + 2 * e + 1]), c2, nm2), x0, x1);
+                    if (e >= 16 - kEmuPairs && !masked) {
+                        exp2_poly_pair(x0, x1, p0, p1);
+                    } else {
+                        p0 = ex2_approx(x0);
+                        p1 = ex2_approx(x1);
+                    }
+                    sum2[cc] = f2_add(sum2[cc], f2_pack(p0, p1));
                     pk[e] = pack_bf16x2(p0, p1);
                 }
                 tmem_st16(tS + cc * 16, pk);
             }
+            float sum_lo, sum_hi;
+            f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])), sum_lo, sum_hi);
+            const float sum = sum_lo + sum_hi;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();

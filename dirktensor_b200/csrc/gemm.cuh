@@ -6,12 +6,15 @@
 // Q/K/V and :103-105 for O).  W keeps the checkpoint's [out, in] row-major
 // layout, which is exactly a K-major B operand, so no transpose is needed.
 //
-// Tile 128 x 256 x 64 (one 128-byte swizzle span of bf16 along K), a 4-stage
-// TMA ring (48 KB per stage), one tcgen05.mma of 128x256x16 per 16-wide K
-// step, accumulator in 256 TMEM columns.
+// Persistent kernel: one CTA per SM walks the 128 x 256 output tiles
+// (tile t, t + gridDim.x, ...; N varies fastest so the CTAs of one wave share
+// their A row panels in L2).  A 4-stage TMA ring (48 KB per stage) feeds one
+// 128x256x16 tcgen05.mma per 16-wide K step.  Two accumulators of 256 TMEM
+// columns alternate between tiles, so the epilogue of tile i (TMEM ->
+// registers -> global) runs while the MMAs of tile i+1 proceed.
 //   warp 0      TMA producer
 //   warp 1      MMA issuer (one thread) and TMEM owner
-//   warps 2-5   epilogue: TMEM -> registers -> global (one row per thread)
+//   warps 2-5   epilogue (one output row per thread, TMEM lane quarter = warp % 4)
 // A may also be "planar": a_planes arrays [M, a_plane_k] stored back to back,
 // forming A[m, p*a_plane_k + x] = plane_p[m, x].  That is the layout in which
 // an all-to-all delivers a token slice of the per-head attention outputs from
@@ -30,6 +33,7 @@ constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
 constexpr int kThreads = 192;
+constexpr int kAccs = 2;                // TMEM accumulators (2 x 256 columns)
 
 struct Params {
     int M, N, K;
@@ -37,6 +41,8 @@ struct Params {
     long long ldc;      // elements
     int c_bf16;         // 0: fp32, 1: bf16
     int a_plane_k;      // 0: A is [M, K]; else A is planar with planes of this K extent
+    int tiles_n;        // ceil(N / kBN)
+    int num_tiles;      // tiles_m * tiles_n
 };
 
 struct __align__(1024) Smem {
@@ -44,12 +50,45 @@ struct __align__(1024) Smem {
     uint8_t b[kStages][kBBytes];
     uint64_t full[kStages];
     uint64_t empty[kStages];
-    uint64_t acc_full;
+    uint64_t acc_full[kAccs];
+    uint64_t acc_empty[kAccs];
     uint64_t mma_done;
     uint32_t tmem_base;
 };
 
-enum : unsigned { kSiteEmpty = 0x21, kSiteFull, kSiteAcc, kSiteDone };
+enum : unsigned { kSiteEmpty = 0x21, kSiteFull, kSiteAcc, kSiteDone, kSiteAccEmpty };
+
+__device__ __forceinline__ void store_chunk(const Params& p, int row, int col, const float (&v)[32]) {
+    if (row >= p.M || col >= p.N) return;
+    if (col + 32 <= p.N) {
+        if (p.c_bf16) {
+            uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)row * p.ldc + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint4 w;
+                w.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+                w.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+                w.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+                w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+                d[i] = w;
+            }
+        } else {
+            float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + (long long)row * p.ldc + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            if (col + e < p.N) {
+                if (p.c_bf16)
+                    reinterpret_cast<__nv_bfloat16*>(p.C)[(long long)row * p.ldc + col + e] = __float2bfloat16_rn(v[e]);
+                else
+                    reinterpret_cast<float*>(p.C)[(long long)row * p.ldc + col + e] = v[e];
+            }
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -58,8 +97,6 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kBN;
-    const int m0 = blockIdx.y * kBM;
     const int nk = (p.K + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
@@ -67,12 +104,15 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        mbar_init(&sm.acc_full, 1);
+        for (int a = 0; a < kAccs; ++a) {
+            mbar_init(&sm.acc_full[a], 1);
+            mbar_init(&sm.acc_empty[a], 4);  // one arrive per epilogue warp
+        }
         mbar_init(&sm.mma_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(&sm.tmem_base, kBN);
+        tmem_alloc(&sm.tmem_base, kAccs * kBN);
         tmem_relinquish();
     }
     if (warp == 0 && lane == 0) {
@@ -85,95 +125,83 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     const uint32_t tmem = sm.tmem_base;
 
     if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStages;
-                const uint32_t ph = (kb / kStages) & 1;
-                if (!mbar_wait(&sm.empty[s], ph ^ 1, kSiteEmpty)) break;
-                mbar_arrive_expect_tx(&sm.full[s], kABytes + kBBytes);
-                if (p.a_plane_k) {
-                    const int plane = (kb * kBK) / p.a_plane_k;
-                    tma_load_3d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK - plane * p.a_plane_k, m0, plane);
-                } else {
-                    tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK, m0);
+            int kit = 0;  // k-blocks issued by this CTA (ring position)
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+                const int m0 = (t / p.tiles_n) * kBM;
+                const int n0 = (t % p.tiles_n) * kBN;
+                for (int kb = 0; kb < nk; ++kb, ++kit) {
+                    const int s = kit % kStages;
+                    if (!mbar_wait(&sm.empty[s], ((kit / kStages) & 1) ^ 1, kSiteEmpty)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&sm.full[s], kABytes + kBBytes);
+                    if (p.a_plane_k) {
+                        const int plane = (kb * kBK) / p.a_plane_k;
+                        tma_load_3d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK - plane * p.a_plane_k, m0, plane);
+                    } else {
+                        tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK, m0);
+                    }
+                    tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * kBK, n0);
                 }
-                tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * kBK, n0);
-                ++issued;
             }
-            if (error_raised())
-                for (int kb = max(0, issued - kStages); kb < issued; ++kb)
-                    mbar_wait(&sm.full[kb % kStages], (kb / kStages) & 1, kSiteFull);
+            if (!ok)  // drain copies still in flight before the CTA exits
+                for (int k = max(0, kit - kStages); k < kit; ++k)
+                    mbar_wait(&sm.full[k % kStages], (k / kStages) & 1, kSiteFull);
         }
     } else if (warp == 1) {
+        // ------------------------------ MMA issuer --------------------------
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_bf16(kBM, kBN, 0, 0);
+            int kit = 0, it = 0;
             bool ok = true;
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % kStages;
-                if (!mbar_wait(&sm.full[s], (kb / kStages) & 1, kSiteFull)) { ok = false; break; }
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++it) {
+                const int acc = it & 1;
+                // the epilogue must have drained this accumulator (used two tiles ago)
+                if (!mbar_wait(&sm.acc_empty[acc], ((it >> 1) & 1) ^ 1, kSiteAccEmpty)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sm.a[s]);
-                const uint32_t b0 = smem_u32(sm.b[s]);
+                const uint32_t d = tmem + acc * kBN;
+                for (int kb = 0; kb < nk; ++kb, ++kit) {
+                    const int s = kit % kStages;
+                    if (!mbar_wait(&sm.full[s], (kit / kStages) & 1, kSiteFull)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sm.a[s]);
+                    const uint32_t b0 = smem_u32(sm.b[s]);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk)
-                    umma_ss(tmem, umma_desc_sw128(a0 + kk * 32, 16, 1024), umma_desc_sw128(b0 + kk * 32, 16, 1024),
-                            idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&sm.empty[s]);
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_ss(d, umma_desc_sw128(a0 + kk * 32, 16, 1024), umma_desc_sw128(b0 + kk * 32, 16, 1024),
+                                idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&sm.empty[s]);
+                }
+                if (ok) umma_commit(&sm.acc_full[acc]);
             }
-            if (ok) umma_commit(&sm.acc_full);
             umma_commit(&sm.mma_done);
             mbar_wait(&sm.mma_done, 0, kSiteDone);
         }
         __syncwarp();
     } else {
-        // epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
+        // -------------------------------- epilogue --------------------------
         const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-        if (mbar_wait(&sm.acc_full, 0, kSiteAcc)) {
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        int it = 0;
+        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+            const int acc = it & 1;
+            if (!mbar_wait(&sm.acc_full[acc], (it >> 1) & 1, kSiteAcc)) break;
             tc_fence_after();
+            const int row = (t / p.tiles_n) * kBM + q * 32 + lane;
+            const int n0 = (t % p.tiles_n) * kBN;
+            const uint32_t taddr = tmem + lane_off + acc * kBN;
 #pragma unroll 1
             for (int cc = 0; cc < kBN / 32; ++cc) {
                 float v[32];
                 tmem_ld32(taddr + cc * 32, v);
                 tmem_wait_ld();
-                const int col = n0 + cc * 32;
-                if (row < p.M && col < p.N) {
-                    if (col + 32 <= p.N) {
-                        if (p.c_bf16) {
-                            uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.C) +
-                                                                (long long)row * p.ldc + col);
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                uint4 w;
-                                w.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
-                                w.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
-                                w.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
-                                w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-                                d[i] = w;
-                            }
-                        } else {
-                            float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) +
-                                                                  (long long)row * p.ldc + col);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            if (col + e < p.N) {
-                                if (p.c_bf16)
-                                    reinterpret_cast<__nv_bfloat16*>(p.C)[(long long)row * p.ldc + col + e] =
-                                        __float2bfloat16_rn(v[e]);
-                                else
-                                    reinterpret_cast<float*>(p.C)[(long long)row * p.ldc + col + e] = v[e];
-                            }
-                        }
-                    }
-                }
+                store_chunk(p, row, n0 + cc * 32, v);
             }
+            // accumulator drained: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
         }
     }
 
@@ -181,7 +209,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kBN);
+        tmem_dealloc(tmem, kAccs * kBN);
     }
 }
 
