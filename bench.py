@@ -200,6 +200,8 @@ def main():
     ap.add_argument("--impl", default="dirktensor", choices=["dirktensor", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="nccl", choices=["fused", "nccl"],
+                    help="N>1: NCCL all-to-all (default) or fused flash + NVLink stores")
     ap.add_argument("--case", default=None, choices=["flash_bf16", "layer"],
                     help="profiling case for ncu: a few launches of one stage, no timing")
     ap.add_argument("--sweep", action="store_true",
@@ -239,7 +241,7 @@ def main():
     v = torch.randn((B, T, Hl, D), generator=gen, device=dev)
     gen.manual_seed(args.seed * 1000 + 999)
     wo = torch.randn((DM, DM), generator=gen, device=dev) * 0.02
-    hp = HeadParallelAttention(wo, n_heads=H, head_dim=D)
+    hp = HeadParallelAttention(wo, n_heads=H, head_dim=D, exchange=args.exchange)
 
     def barrier():
         if world > 1:
@@ -350,8 +352,9 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "config4_head_parallel_attention", "B": B, "T": T, "H": H, "D": D,
-                       "d_model": DM, "causal": True, "parallelism": f"head-parallel x{world} + token-sliced "
-                       "all-to-all + O-proj", "flops_per_step": flops_step,
+                       "d_model": DM, "causal": True,
+                       "parallelism": f"head-parallel x{world} + token-sliced exchange ({args.exchange}) + O-proj",
+                       "flops_per_step": flops_step,
                        "l2": "inputs larger than L2 (805 MB fp32 per tensor in total)"},
             "prefill_tok_s": M / (ms_step * 1e-3),
             "roofline": {"bound": "tensor", "kernel": "flash_fwd_kernel", "achieved": achieved, "peak": peak,
@@ -365,6 +368,7 @@ def main():
             "layers": layers,
         }
         print(json.dumps(line), flush=True)
+    hp.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

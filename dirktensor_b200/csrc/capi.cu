@@ -17,6 +17,7 @@
 #include "dt_common.cuh"
 #include "flash_fwd.cuh"
 #include "gemm.cuh"
+#include "model.cuh"
 #include "prologue.cuh"
 
 namespace {
@@ -261,15 +262,22 @@ int launch_cast3(const float* a, const float* b, const float* c, void* da, void*
     return DT_OK;
 }
 
+struct Scatter {
+    int ranks = 0;
+    int plane = 0;
+    long long tokens_per_rank = 0;
+    void* const* dst = nullptr;
+};
+
 int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
                  float* m, float* l, const int* seq_lens, int B, int T, int H, float scale, int causal,
-                 cudaStream_t st) {
+                 cudaStream_t st, const Scatter& sc = Scatter()) {
     if ((long long)B * T * H == 0) return DT_OK;
     CUtensorMap mq, mk, mv;
     DT_TRY(make_map_bthd(&mq, q, B, T, H, 128));
     DT_TRY(make_map_bthd(&mk, k, B, T, H, 128));
     DT_TRY(make_map_bthd(&mv, v, B, T, H, 128));
-    dt::flash::Params p;
+    dt::flash::Params p{};
     p.B = B;
     p.T = T;
     p.H = H;
@@ -302,6 +310,10 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     p.m_out = m;
     p.l_out = l;
     p.seq_lens = seq_lens;
+    p.scatter_ranks = sc.ranks;
+    p.scatter_plane = sc.plane;
+    p.tokens_per_rank = sc.tokens_per_rank;
+    for (int r = 0; r < 8; ++r) p.scatter_dst[r] = (r < sc.ranks) ? sc.dst[r] : nullptr;
     const long long grid = (long long)p.nblk * B * H;
     if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
     dt::flash::flash_fwd_kernel<<<(unsigned)grid, dt::flash::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
@@ -310,14 +322,14 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
 }
 
 int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N, int K, long long ldc,
-                cudaStream_t st, int a_planes = 1) {
+                cudaStream_t st, int a_planes = 1, int epilogue = dt::gemm::kStore) {
     if (M == 0 || N == 0) return DT_OK;
     CUtensorMap ma, mb;
     const int plane_k = K / a_planes;
     if (a_planes > 1) DT_TRY(make_map_planar(&ma, A, M, plane_k, a_planes));
     else DT_TRY(make_map_2d(&ma, A, M, K, dt::gemm::kBM));
     DT_TRY(make_map_2d(&mb, Bm, N, K, dt::gemm::kBN));
-    dt::gemm::Params p;
+    dt::gemm::Params p{};
     p.M = M;
     p.N = N;
     p.K = K;
@@ -325,6 +337,7 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     p.ldc = ldc;
     p.c_bf16 = c_bf16;
     p.a_plane_k = a_planes > 1 ? plane_k : 0;
+    p.epilogue = epilogue;
     p.tiles_n = (N + dt::gemm::kBN - 1) / dt::gemm::kBN;
     const long long tiles = (long long)p.tiles_n * ((M + dt::gemm::kBM - 1) / dt::gemm::kBM);
     if (tiles > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "GEMM too large");
@@ -571,6 +584,76 @@ int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int 
                         causal, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int dt_flash_fwd_bf16_exchange(const void* q, const void* k, const void* v, void* const* recv_bufs, int ranks,
+                               int rank, long long tokens_per_rank, float* softmax_m, float* softmax_l, int B, int T,
+                               int H, int D, float scale, int causal, void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (ranks < 1 || ranks > 8 || rank < 0 || rank >= ranks)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ranks must be 1..8 and 0 <= rank < ranks");
+    if (!recv_bufs || tokens_per_rank <= 0 || tokens_per_rank * ranks != (long long)B * T)
+        return fail(DT_ERR_INVALID_ARGUMENT, "tokens_per_rank * ranks must equal B*T");
+    if (!q || !k || !v || !aligned16(q) || !aligned16(k) || !aligned16(v))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v must be non-null and 16-byte aligned");
+    for (int r = 0; r < ranks; ++r)
+        if (!recv_bufs[r] || !aligned16(recv_bufs[r]))
+            return fail(DT_ERR_INVALID_ARGUMENT, "receive buffer %d must be non-null and 16-byte aligned", r);
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    Scatter sc;
+    sc.ranks = ranks;
+    sc.plane = rank;
+    sc.tokens_per_rank = tokens_per_rank;
+    sc.dst = recv_bufs;
+    return launch_flash(q, k, v, nullptr, 1, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale,
+                        causal, reinterpret_cast<cudaStream_t>(stream), sc);
+}
+
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int dt_ipc_get_handle(const void* dev_ptr, void* handle_out, size_t* offset_out) {
+    t_last_error.clear();
+    if (!dev_ptr || !handle_out || !offset_out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    // The handle names the whole allocation; a caching allocator may hand out
+    // an interior pointer, so report its offset from the allocation base.
+    static AddressRangeFn range = nullptr;
+    if (!range) {
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", reinterpret_cast<void**>(&range), cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !range)
+            return fail(DT_ERR_CUDA, "cuMemGetAddressRange unavailable");
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return fail(DT_ERR_INVALID_ARGUMENT, "pointer is not a device allocation");
+    cudaIpcMemHandle_t h;
+    DT_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    std::memcpy(handle_out, &h, sizeof(h));
+    *offset_out = reinterpret_cast<uintptr_t>(dev_ptr) - static_cast<uintptr_t>(base);
+    return DT_OK;
+}
+
+int dt_ipc_open(const void* handle, size_t offset, void** dev_ptr_out) {
+    t_last_error.clear();
+    if (!handle || !dev_ptr_out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    DT_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    *dev_ptr_out = static_cast<uint8_t*>(base) + offset;
+    return DT_OK;
+}
+
+int dt_ipc_close(void* dev_ptr, size_t offset) {
+    t_last_error.clear();
+    if (!dev_ptr) return DT_OK;
+    DT_CUDA(cudaIpcCloseMemHandle(static_cast<uint8_t*>(dev_ptr) - offset));
+    return DT_OK;
+}
+
 int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream) {
     t_last_error.clear();
     if (n < 0 || (n % 4) != 0) return fail(DT_ERR_INVALID_ARGUMENT, "n must be a non-negative multiple of 4");
@@ -796,8 +879,35 @@ int dt_attn_destroy(dt_attn* a) {
     return DT_OK;
 }
 
+// Scratch of attn_core for M tokens: [q|k|v] fp32 and four bf16 [M, d] arrays.
+static size_t attn_core_bytes(long long M) { return align256(M * 6144 * 4) + 4 * align256(M * 2048 * 2); }
+
+// OlmoAttention::forward on a bf16 input (OlmoAttention.cpp:56-108): fused QKV
+// GEMM, QK-norm + RoPE prologue, flash attention, O projection into y (fp32).
+static int attn_core(dt_attn* a, const void* xb, int B, int T, const int* seq_lens, float* y, uint8_t* ws, int dev,
+                     cudaStream_t st) {
+    const long long M = (long long)B * T;
+    const int d = a->d_model;
+    const size_t act = align256(M * d * 2);
+    float* qkv = reinterpret_cast<float*>(ws);
+    uint8_t* rest = ws + align256(M * 3 * d * 4);
+    void* qb = rest;
+    void* kb = rest + act;
+    void* vb = rest + 2 * act;
+    void* ab = rest + 3 * act;
+    const float *sin_t, *cos_t;
+    DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
+    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st));         // [q|k|v] = x Wqkv^T
+    DT_TRY(launch_prologue(qkv, qkv + d, qkv + 2 * d, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
+                           st));                                                    // norm + RoPE
+    DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, nullptr, nullptr, seq_lens, B, T, a->n_heads,
+                        1.0f / std::sqrt(128.0f), 1, st));                          // attention
+    DT_TRY(launch_gemm(ab, a->wo, y, 0, (int)M, d, d, d, st));                     // y = a Wo^T
+    return DT_OK;
+}
+
 static int attn_workspace(dt_attn* a, long long M, uint8_t** ws) {
-    const size_t need = align256(M * 2048 * 2) * 5 + align256(M * 6144 * 4);
+    const size_t need = align256(M * 2048 * 2) + attn_core_bytes(M);
     if (a->ws_bytes < need) {
         if (a->ws) DT_CUDA(cudaFree(a->ws));
         a->ws = nullptr;
@@ -826,24 +936,9 @@ int dt_attn_forward(dt_attn* a, const float* x, int B, int T, const int* seq_len
     const int d = a->d_model;
     uint8_t* ws;
     DT_TRY(attn_workspace(a, M, &ws));
-    const size_t act = align256(M * d * 2);
     void* xb = ws;
-    float* qkv = reinterpret_cast<float*>(ws + act);
-    uint8_t* rest = ws + act + align256(M * 3 * d * 4);
-    void* qb = rest;
-    void* kb = rest + act;
-    void* vb = rest + 2 * act;
-    void* ab = rest + 3 * act;
-    const float *sin_t, *cos_t;
-    DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
-    DT_TRY(launch_cast(x, xb, M * d, st));                                         // x -> bf16
-    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st));         // [q|k|v] = x Wqkv^T
-    DT_TRY(launch_prologue(qkv, qkv + d, qkv + 2 * d, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
-                           st));                                                    // norm + RoPE
-    DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, nullptr, nullptr, seq_lens, B, T, a->n_heads,
-                        1.0f / std::sqrt(128.0f), 1, st));                          // attention
-    DT_TRY(launch_gemm(ab, a->wo, y, 0, (int)M, d, d, d, st));                     // y = a Wo^T
-    return DT_OK;
+    DT_TRY(launch_cast(x, xb, M * d, st));  // x -> bf16
+    return attn_core(a, xb, B, T, seq_lens, y, ws + align256(M * d * 2), dev, st);
 }
 
 int dt_attn_forward_host(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y) {
@@ -873,6 +968,293 @@ int dt_attn_forward_host(dt_attn* a, const float* x, int B, int T, const int* se
     DT_TRY(dt_attn_forward(a, dx, B, T, seq_lens ? dl : nullptr, dy, a->stream));
     DT_CUDA(cudaMemcpyAsync(y, dy, (size_t)M * a->d_model * 4, cudaMemcpyDeviceToHost, a->stream));
     DT_CUDA(cudaStreamSynchronize(a->stream));
+    bool had;
+    return read_device_error(&had);
+}
+
+
+// ---- full model prefill (configuration 3) ------------------------------------
+
+struct dt_model {
+    int device = 0;
+    int n_layers = 0, vocab = 0, d_model = 0, n_heads = 0, hidden = 0;
+    float eps = 1e-6f, theta = 500000.f;
+    float* embed = nullptr;              // [vocab, d] fp32 (gathered into the fp32 residual stream)
+    __nv_bfloat16* lm_head = nullptr;    // [vocab, d]
+    float* final_norm = nullptr;         // [d]
+    std::vector<dt_attn*> attn;          // per layer: Wqkv, Wo, q/k norm gains
+    std::vector<float*> pa_norm, pf_norm;
+    std::vector<__nv_bfloat16*> w_gu;    // [2*hidden, d], gate/up interleaved in 128-row blocks
+    std::vector<__nv_bfloat16*> w_down;  // [d, hidden]
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    void* io = nullptr;
+    size_t io_bytes = 0;
+    cudaStream_t stream = nullptr;
+};
+
+static int upload_bf16(const float* host, size_t n, __nv_bfloat16** out, float* stage) {
+    DT_CUDA(cudaMalloc(out, n * 2));
+    DT_CUDA(cudaMemcpy(stage, host, n * 4, cudaMemcpyHostToDevice));
+    DT_TRY(launch_cast(stage, *out, (long long)n, nullptr));
+    DT_CUDA(cudaDeviceSynchronize());
+    return DT_OK;
+}
+
+static int upload_f32(const float* host, size_t n, float** out) {
+    DT_CUDA(cudaMalloc(out, n * 4));
+    DT_CUDA(cudaMemcpy(*out, host, n * 4, cudaMemcpyHostToDevice));
+    return DT_OK;
+}
+
+static int model_upload(dt_model* m, const dt_model_weights* w) {
+    const int d = m->d_model, hid = m->hidden;
+    const size_t stage_n = std::max((size_t)m->vocab * d, (size_t)2 * hid * d);
+    float* stage = nullptr;
+    DT_CUDA(cudaMalloc(&stage, stage_n * 4));
+    int s = DT_OK;
+    do {
+        if ((s = upload_f32(w->embed, (size_t)m->vocab * d, &m->embed)) != DT_OK) break;
+        if ((s = upload_bf16(w->lm_head, (size_t)m->vocab * d, &m->lm_head, stage)) != DT_OK) break;
+        if ((s = upload_f32(w->final_norm, d, &m->final_norm)) != DT_OK) break;
+        for (int l = 0; l < m->n_layers && s == DT_OK; ++l) {
+            const dt_model_layer_weights& L = w->layers[l];
+            dt_attn_weights aw;
+            aw.q_proj = L.q_proj;
+            aw.k_proj = L.k_proj;
+            aw.v_proj = L.v_proj;
+            aw.o_proj = L.o_proj;
+            aw.q_norm = L.q_norm;
+            aw.k_norm = L.k_norm;
+            aw.d_model = d;
+            aw.n_heads = m->n_heads;
+            aw.eps = m->eps;
+            aw.rope_theta = m->theta;
+            dt_attn* a = nullptr;
+            if ((s = dt_attn_create(&aw, m->device, &a)) != DT_OK) break;
+            m->attn.push_back(a);
+            float *pa = nullptr, *pf = nullptr;
+            if ((s = upload_f32(L.post_attention_norm, d, &pa)) != DT_OK) break;
+            m->pa_norm.push_back(pa);
+            if ((s = upload_f32(L.post_feedforward_norm, d, &pf)) != DT_OK) break;
+            m->pf_norm.push_back(pf);
+            // gate/up interleaved by 128-row blocks: rows [256b, 256b+128) = gate block b,
+            // rows [256b+128, 256b+256) = up block b
+            const size_t blk = (size_t)128 * d;
+            cudaError_t e = cudaMemcpy2D(stage, 2 * blk * 4, L.gate_proj, blk * 4, blk * 4, hid / 128,
+                                         cudaMemcpyHostToDevice);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2D(stage + blk, 2 * blk * 4, L.up_proj, blk * 4, blk * 4, hid / 128,
+                                 cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) { s = fail(DT_ERR_CUDA, "uploading MLP weights: %s", cudaGetErrorString(e)); break; }
+            __nv_bfloat16* gu = nullptr;
+            e = cudaMalloc(&gu, (size_t)2 * hid * d * 2);
+            if (e != cudaSuccess) { s = fail(DT_ERR_OUT_OF_MEMORY, "cudaMalloc: %s", cudaGetErrorString(e)); break; }
+            m->w_gu.push_back(gu);
+            if ((s = launch_cast(stage, gu, (long long)2 * hid * d, nullptr)) != DT_OK) break;
+            __nv_bfloat16* dn = nullptr;
+            if ((s = upload_bf16(L.down_proj, (size_t)d * hid, &dn, stage)) != DT_OK) break;
+            m->w_down.push_back(dn);
+        }
+    } while (false);
+    cudaDeviceSynchronize();
+    cudaFree(stage);
+    return s;
+}
+
+int dt_model_destroy(dt_model* m) {
+    if (!m) return DT_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->device);
+    for (dt_attn* a : m->attn) dt_attn_destroy(a);
+    for (float* x : m->pa_norm) cudaFree(x);
+    for (float* x : m->pf_norm) cudaFree(x);
+    for (__nv_bfloat16* x : m->w_gu) cudaFree(x);
+    for (__nv_bfloat16* x : m->w_down) cudaFree(x);
+    cudaFree(m->embed);
+    cudaFree(m->lm_head);
+    cudaFree(m->final_norm);
+    cudaFree(m->ws);
+    cudaFree(m->io);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    cudaSetDevice(prev);
+    delete m;
+    return DT_OK;
+}
+
+int dt_model_create(const dt_model_weights* w, int device, dt_model** out) {
+    t_last_error.clear();
+    if (!w || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (w->d_model != 2048 || w->n_heads <= 0 || w->d_model / w->n_heads != 128 || w->d_model % w->n_heads)
+        return fail(DT_ERR_UNSUPPORTED, "need d_model 2048 and head_dim 128");
+    if (w->n_layers <= 0 || w->vocab <= 0 || w->hidden <= 0 || (w->hidden % 128) != 0 || (w->vocab % 8) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "need n_layers, vocab (multiple of 8), hidden (multiple of 128) > 0");
+    if (!w->embed || !w->final_norm || !w->lm_head || !w->layers) return fail(DT_ERR_INVALID_ARGUMENT, "null weights");
+    for (int l = 0; l < w->n_layers; ++l) {
+        const dt_model_layer_weights& L = w->layers[l];
+        if (!L.q_proj || !L.k_proj || !L.v_proj || !L.o_proj || !L.q_norm || !L.k_norm || !L.post_attention_norm ||
+            !L.gate_proj || !L.up_proj || !L.down_proj || !L.post_feedforward_norm)
+            return fail(DT_ERR_INVALID_ARGUMENT, "null weight pointer in layer %d", l);
+    }
+    DT_CUDA(cudaSetDevice(device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    dt_model* m = new dt_model();
+    m->device = device;
+    m->n_layers = w->n_layers;
+    m->vocab = w->vocab;
+    m->d_model = w->d_model;
+    m->n_heads = w->n_heads;
+    m->hidden = w->hidden;
+    m->eps = w->eps;
+    m->theta = w->rope_theta;
+    const int s = model_upload(m, w);
+    if (s != DT_OK) {
+        std::string msg = t_last_error;
+        dt_model_destroy(m);
+        t_last_error = msg;
+        return s;
+    }
+    *out = m;
+    return DT_OK;
+}
+
+int dt_model_create_from_npy(const char* folder, int n_layers, int device, dt_model** out) {
+    t_last_error.clear();
+    if (!folder || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    if (n_layers <= 0) n_layers = 16;
+    const std::string f(folder);
+    std::vector<std::vector<float>> store;
+    store.reserve(3 + 11 * (size_t)n_layers);
+    auto load = [&](const std::string& path, const float** dst, std::vector<long long>* shape_out) -> int {
+        store.emplace_back();
+        std::vector<long long> shape;
+        DT_TRY(read_npy_f32(path, store.back(), shape));
+        if (shape_out) *shape_out = shape;
+        *dst = store.back().data();
+        return DT_OK;
+    };
+    dt_model_weights w;
+    std::vector<long long> es;
+    DT_TRY(load(f + "/model.embed_tokens.weight.npy", &w.embed, &es));
+    DT_TRY(load(f + "/model.norm.weight.npy", &w.final_norm, nullptr));
+    std::vector<long long> ls;
+    DT_TRY(load(f + "/lm_head.weight.npy", &w.lm_head, &ls));
+    if (es.size() != 2 || ls.size() != 2 || es[1] != 2048 || ls[1] != 2048 || es[0] != ls[0])
+        return fail(DT_ERR_IO, "embedding / lm_head shapes must be [vocab, 2048]");
+    std::vector<dt_model_layer_weights> layers(n_layers);
+    std::vector<long long> us;
+    for (int l = 0; l < n_layers; ++l) {
+        const std::string pre = f + "/model.layers." + std::to_string(l) + ".";
+        dt_model_layer_weights& L = layers[l];
+        DT_TRY(load(pre + "self_attn.q_proj.weight.npy", &L.q_proj, nullptr));
+        DT_TRY(load(pre + "self_attn.k_proj.weight.npy", &L.k_proj, nullptr));
+        DT_TRY(load(pre + "self_attn.v_proj.weight.npy", &L.v_proj, nullptr));
+        DT_TRY(load(pre + "self_attn.o_proj.weight.npy", &L.o_proj, nullptr));
+        DT_TRY(load(pre + "self_attn.q_norm.weight.npy", &L.q_norm, nullptr));
+        DT_TRY(load(pre + "self_attn.k_norm.weight.npy", &L.k_norm, nullptr));
+        DT_TRY(load(pre + "post_attention_layernorm.weight.npy", &L.post_attention_norm, nullptr));
+        DT_TRY(load(pre + "mlp.gate_proj.weight.npy", &L.gate_proj, nullptr));
+        DT_TRY(load(pre + "mlp.up_proj.weight.npy", &L.up_proj, &us));
+        DT_TRY(load(pre + "mlp.down_proj.weight.npy", &L.down_proj, nullptr));
+        DT_TRY(load(pre + "post_feedforward_layernorm.weight.npy", &L.post_feedforward_norm, nullptr));
+    }
+    w.layers = layers.data();
+    w.n_layers = n_layers;
+    w.vocab = (int)es[0];
+    w.d_model = 2048;
+    w.n_heads = 16;
+    w.hidden = us.size() == 2 ? (int)us[0] : 8192;
+    w.eps = 1e-6f;
+    w.rope_theta = 500000.f;
+    return dt_model_create(&w, device, out);
+}
+
+static size_t model_ws_bytes(const dt_model* m, long long M) {
+    return 2 * align256(M * m->d_model * 4) + align256(M * m->d_model * 2) + attn_core_bytes(M) +
+           align256(M * m->hidden * 2);
+}
+
+int dt_model_forward(dt_model* m, const uint32_t* tokens, int B, int T, float* logits, void* stream) {
+    t_last_error.clear();
+    if (!m) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    if (T > kMaxSeqLen) return fail(DT_ERR_INVALID_ARGUMENT, "T=%d exceeds max_seq_len %d", T, kMaxSeqLen);
+    const long long M = (long long)B * T;
+    if (M == 0) return DT_OK;
+    if (!tokens || !logits || !aligned16(logits)) return fail(DT_ERR_INVALID_ARGUMENT, "tokens/logits invalid");
+    DT_CUDA(cudaSetDevice(m->device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    const size_t need = model_ws_bytes(m, M);
+    if (m->ws_bytes < need) {
+        if (m->ws) DT_CUDA(cudaFree(m->ws));
+        m->ws = nullptr;
+        m->ws_bytes = 0;
+        DT_CUDA(cudaMalloc(&m->ws, need));
+        m->ws_bytes = need;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int d = m->d_model;
+    uint8_t* w = reinterpret_cast<uint8_t*>(m->ws);
+    float* x = reinterpret_cast<float*>(w);
+    w += align256(M * d * 4);
+    float* y = reinterpret_cast<float*>(w);
+    w += align256(M * d * 4);
+    __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(w);
+    w += align256(M * d * 2);
+    uint8_t* attn_ws = w;
+    w += attn_core_bytes(M);
+    __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(w);
+    const unsigned rows = (unsigned)M;
+    dt::model::embed_gather_kernel<<<rows, dt::model::kThreads, 0, st>>>(tokens, m->embed, m->vocab, x, xb);
+    DT_CUDA(cudaGetLastError());
+    for (int l = 0; l < m->n_layers; ++l) {
+        DT_TRY(attn_core(m->attn[l], xb, B, T, nullptr, y, attn_ws, dev, st));                  // attention
+        dt::model::residual_norm_kernel<<<rows, dt::model::kThreads, 0, st>>>(x, y, m->pa_norm[l], x, xb, m->eps, 1);
+        DT_CUDA(cudaGetLastError());                                                            // h = x + norm(attn)
+        DT_TRY(launch_gemm(xb, m->w_gu[l], act, 1, (int)M, 2 * m->hidden, d, m->hidden, st, 1,
+                           dt::gemm::kSwiGLU));                                                 // silu(g) * u
+        DT_TRY(launch_gemm(act, m->w_down[l], y, 0, (int)M, d, m->hidden, d, st));             // down
+        dt::model::residual_norm_kernel<<<rows, dt::model::kThreads, 0, st>>>(x, y, m->pf_norm[l], x, xb, m->eps, 1);
+        DT_CUDA(cudaGetLastError());                                                            // x = h + norm(mlp)
+    }
+    dt::model::residual_norm_kernel<<<rows, dt::model::kThreads, 0, st>>>(nullptr, x, m->final_norm, nullptr, xb,
+                                                                          m->eps, 0);          // final norm
+    DT_CUDA(cudaGetLastError());
+    return launch_gemm(xb, m->lm_head, logits, 0, (int)M, m->vocab, d, m->vocab, st);           // LM head
+}
+
+int dt_model_forward_host(dt_model* m, const uint32_t* tokens, int B, int T, float* logits) {
+    t_last_error.clear();
+    if (!m) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    const long long M = (long long)B * T;
+    if (M == 0) return DT_OK;
+    if (!tokens || !logits) return fail(DT_ERR_INVALID_ARGUMENT, "null tokens/logits");
+    for (long long i = 0; i < M; ++i)
+        if (tokens[i] >= (uint32_t)m->vocab)
+            return fail(DT_ERR_INVALID_ARGUMENT, "token id %u at position %lld is not below the vocabulary size %d",
+                        tokens[i], i, m->vocab);
+    DT_CUDA(cudaSetDevice(m->device));
+    if (!m->stream) DT_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    const size_t lb = align256((size_t)M * m->vocab * 4);
+    const size_t need = lb + align256((size_t)M * 4);
+    if (m->io_bytes < need) {
+        if (m->io) DT_CUDA(cudaFree(m->io));
+        m->io = nullptr;
+        m->io_bytes = 0;
+        DT_CUDA(cudaMalloc(&m->io, need));
+        m->io_bytes = need;
+    }
+    float* dl = reinterpret_cast<float*>(m->io);
+    uint32_t* dt_ids = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(m->io) + lb);
+    DT_CUDA(cudaMemcpyAsync(dt_ids, tokens, (size_t)M * 4, cudaMemcpyHostToDevice, m->stream));
+    DT_TRY(dt_model_forward(m, dt_ids, B, T, dl, m->stream));
+    DT_CUDA(cudaMemcpyAsync(logits, dl, (size_t)M * m->vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    DT_CUDA(cudaStreamSynchronize(m->stream));
     bool had;
     return read_device_error(&had);
 }

@@ -298,6 +298,17 @@ __device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, fl
     y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
+// Per-warpgroup register re-allocation (all 4 warps of a warpgroup execute it).
+// The sum over warpgroups must stay within the CTA's launch allocation.
+template <uint32_t N>
+__device__ __forceinline__ void regs_increase() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_decrease() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

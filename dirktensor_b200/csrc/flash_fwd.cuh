@@ -66,6 +66,15 @@ struct Params {
     float* m_out;           // [B, T, H] or null
     float* l_out;           // [B, T, H] or null
     const int* seq_lens;    // [B] or null; rows t >= seq_lens[b] are written as zeros
+    // Exchange mode (head-parallel path; scatter_ranks > 0): the row of global
+    // token g = b*T + t is stored into rank r = g / tokens_per_rank's receive
+    // buffer scatter_dst[r] (this GPU's own or a peer's, mapped over NVLink) at
+    // plane scatter_plane (this rank), row g - r*tokens_per_rank; each plane is
+    // [tokens_per_rank, out_row_stride].  `out` is unused then.
+    int scatter_ranks;
+    int scatter_plane;
+    long long tokens_per_rank;
+    void* scatter_dst[8];
 };
 
 struct __align__(1024) Smem {
@@ -86,9 +95,17 @@ enum : unsigned { kSiteQ = 1, kSiteKvEmpty, kSiteKvFull, kSiteS, kSiteP, kSiteO,
 
 // Writes 32 consecutive output columns [col0, col0+32) of row (b, t, h), each multiplied by `mul`.
 __device__ __forceinline__ void store_chunk(const Params& p, int b, int t, int h, int col0, const float* v, float mul) {
-    const long long base = ((long long)b * p.T + t) * p.out_row_stride + (long long)h * kD + col0;
+    const long long g = (long long)b * p.T + t;
+    void* dst = p.out;
+    long long row = g;
+    if (p.scatter_ranks > 0) {
+        const int r = static_cast<int>(g / p.tokens_per_rank);
+        dst = p.scatter_dst[r];
+        row = (long long)p.scatter_plane * p.tokens_per_rank + (g - (long long)r * p.tokens_per_rank);
+    }
+    const long long base = row * p.out_row_stride + (long long)h * kD + col0;
     if (p.out_bf16) {
-        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + base);
+        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + base);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint4 w;
@@ -99,7 +116,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int b, int t, int h
             d4[i] = w;
         }
     } else {
-        float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base);
+        float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + base);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
             d4[i] = make_float4(v[4 * i] * mul, v[4 * i + 1] * mul, v[4 * i + 2] * mul, v[4 * i + 3] * mul);
@@ -387,6 +404,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             if (p.m_out) p.m_out[sidx] = m_o;
             if (p.l_out) p.l_out[sidx] = l_o;
         }
+        // rows stored into peers' memory become visible system-wide before the
+        // caller's stream-ordered barrier lets the owners read them
+        if (p.scatter_ranks > 0) __threadfence_system();
     }
 
     tc_fence_before();

@@ -15,6 +15,11 @@
 //   warp 0      TMA producer
 //   warp 1      MMA issuer (one thread) and TMEM owner
 //   warps 2-5   epilogue (one output row per thread, TMEM lane quarter = warp % 4)
+// Epilogue kSwiGLU (the MLP's gate/up product, OlmoMlp.cpp:38-52): B holds the
+// gate and up weights interleaved in 128-row blocks, so accumulator columns
+// [0,128) of a tile are gate and [128,256) the matching up columns; the
+// epilogue writes silu(gate) * up = gate / (1 + exp(-gate)) * up as bf16 into
+// output columns [128 n, 128 n + 128) (C has N/2 columns).
 // A may also be "planar": a_planes arrays [M, a_plane_k] stored back to back,
 // forming A[m, p*a_plane_k + x] = plane_p[m, x].  That is the layout in which
 // an all-to-all delivers a token slice of the per-head attention outputs from
@@ -43,7 +48,10 @@ struct Params {
     int a_plane_k;      // 0: A is [M, K]; else A is planar with planes of this K extent
     int tiles_n;        // ceil(N / kBN)
     int num_tiles;      // tiles_m * tiles_n
+    int epilogue;       // kStore or kSwiGLU
 };
+
+enum Epilogue : int { kStore = 0, kSwiGLU = 1 };
 
 struct __align__(1024) Smem {
     uint8_t a[kStages][kABytes];
@@ -191,12 +199,43 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             const int row = (t / p.tiles_n) * kBM + q * 32 + lane;
             const int n0 = (t % p.tiles_n) * kBN;
             const uint32_t taddr = tmem + lane_off + acc * kBN;
+            if (p.epilogue == kSwiGLU) {
+                const int oc0 = (t % p.tiles_n) * (kBN / 2);
 #pragma unroll 1
-            for (int cc = 0; cc < kBN / 32; ++cc) {
-                float v[32];
-                tmem_ld32(taddr + cc * 32, v);
-                tmem_wait_ld();
-                store_chunk(p, row, n0 + cc * 32, v);
+                for (int cc = 0; cc < kBN / 64; ++cc) {
+                    float g[32], u[32];
+                    tmem_ld32(taddr + cc * 32, g);
+                    tmem_ld32(taddr + kBN / 2 + cc * 32, u);
+                    tmem_wait_ld();
+                    const int oc = oc0 + cc * 32;
+                    if (row < p.M && oc + 32 <= p.N / 2) {
+                        uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.C) +
+                                                            (long long)row * p.ldc + oc);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            float a[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float x = g[8 * i + e];
+                                a[e] = x / (1.f + __expf(-x)) * u[8 * i + e];
+                            }
+                            uint4 w;
+                            w.x = pack_bf16x2(a[0], a[1]);
+                            w.y = pack_bf16x2(a[2], a[3]);
+                            w.z = pack_bf16x2(a[4], a[5]);
+                            w.w = pack_bf16x2(a[6], a[7]);
+                            d[i] = w;
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int cc = 0; cc < kBN / 32; ++cc) {
+                    float v[32];
+                    tmem_ld32(taddr + cc * 32, v);
+                    tmem_wait_ld();
+                    store_chunk(p, row, n0 + cc * 32, v);
+                }
             }
             // accumulator drained: hand it back to the MMA warp
             tc_fence_before();

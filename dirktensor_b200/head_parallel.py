@@ -14,12 +14,25 @@ Layouts:
   received       [G, M/G, Hl*D] bf16 (plane g = rank g's heads)
   O projection   y[M/G, d] = A . Wo^T with A planar over G planes (plane g holds
                  columns [g*Hl*D, (g+1)*Hl*D) of the concatenated heads)
-The exchange runs through torch.distributed (NCCL on GPUs); the attention and
-projection kernels are the CUDA library's.
+Two exchange modes:
+  nccl (default): the flash kernel writes a local [M, Hl*D] buffer and
+      torch.distributed.all_to_all_single moves the token slices.
+  fused: the flash kernel's epilogue
+      stores each output row straight into the owning rank's receive buffer
+      over NVLink (peer pointers from CUDA IPC, plain stores), i.e. attention and
+      exchange are one kernel; a one-element all-reduce on the same stream then
+      orders every rank's stores before the owners' O projections.  Receive
+      buffers are double-buffered across steps, so a rank that runs ahead never
+      overwrites a buffer its owner is still projecting.  Measured at 2 GPUs
+      (config 4) it is slower than the NCCL path (per-row 16-byte stores to the
+      peer stretch the epilogue), hence not the default.
+The attention and projection kernels are the CUDA library's.
 """
 from __future__ import annotations
 
 from typing import Optional, Tuple
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -52,7 +65,10 @@ class HeadParallelAttention:
     exchange_dtype = torch.bfloat16
 
     def __init__(self, wo: torch.Tensor, n_heads: int = 16, head_dim: int = 128,
-                 group: Optional[dist.ProcessGroup] = None):
+                 group: Optional[dist.ProcessGroup] = None, exchange: str = "nccl"):
+        if exchange not in ("fused", "nccl"):
+            raise ValueError("exchange must be 'fused' or 'nccl'")
+        self.exchange_mode = exchange
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -61,6 +77,8 @@ class HeadParallelAttention:
         self.h0, self.h1 = head_range(self.rank, self.world, n_heads)
         self.wo = self._prepare_wo(wo)
         self._bufs = {}
+        self._fused = None   # (shape, [recv buffers], [peer pointer arrays], [(ptr, offset) opened])
+        self._step = 0
 
     # ---- compute steps (CUDA library) ------------------------------------
     def _prepare_wo(self, wo: torch.Tensor) -> torch.Tensor:
@@ -112,13 +130,82 @@ class HeadParallelAttention:
         dist.all_to_all_single(recv, send, group=self.group)
         return recv
 
+    # ---- fused attention + exchange ------------------------------------------
+    def _setup_fused(self, M: int, w: int, device):
+        """Two receive buffers [G, M/G, w] bf16 per rank; every rank maps every
+        peer's buffers through CUDA IPC (64-byte handles all-gathered once)."""
+        G = self.world
+        shape = (G, M // G, w)
+        if self._fused is not None and self._fused[0] == shape:
+            return
+        self.close()
+        L = lib()
+        recv = [torch.empty(shape, dtype=torch.bfloat16, device=device) for _ in range(2)]
+        mine = torch.zeros((2, 72), dtype=torch.uint8)
+        for i, buf in enumerate(recv):
+            h = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_size_t()
+            check(L.dt_ipc_get_handle(buf.data_ptr(), h, ctypes.byref(off)))
+            mine[i, :64] = torch.tensor(list(bytes(h)), dtype=torch.uint8)
+            mine[i, 64:] = torch.tensor(list(off.value.to_bytes(8, "little")), dtype=torch.uint8)
+        allh = torch.empty((G, 2, 72), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(allh, mine.to(device), group=self.group)
+        allh = allh.cpu()
+        ptrs, opened = [], []
+        for i in range(2):
+            arr = (ctypes.c_void_p * G)()
+            for r in range(G):
+                if r == self.rank:
+                    arr[r] = recv[i].data_ptr()
+                    continue
+                hb = bytes(allh[r, i, :64].tolist())
+                off = int.from_bytes(bytes(allh[r, i, 64:].tolist()), "little")
+                p = ctypes.c_void_p()
+                check(L.dt_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(hb), off, ctypes.byref(p)))
+                arr[r] = p.value
+                opened.append((p.value, off))
+            ptrs.append(arr)
+        self._fused = (shape, recv, ptrs, opened)
+        self._barrier = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def close(self):
+        """Unmaps the peers' receive buffers (fused exchange)."""
+        if self._fused is not None:
+            for ptr, off in self._fused[3]:
+                lib().dt_ipc_close(ctypes.c_void_p(ptr), off)
+            self._fused = None
+
+    def fused_attention_exchange(self, q, k, v, scale: float, causal: bool, events=None) -> torch.Tensor:
+        """One kernel computes this rank's heads and stores every output row in
+        its owner's receive buffer; returns this rank's filled receive buffer."""
+        B, T, Hl, D = q.shape
+        M = B * T
+        self._setup_fused(M, Hl * D, q.device)
+        buf = self._step & 1
+        self._step += 1
+        qb, kb, vb = (_attn.cast_bf16(t) for t in (q, k, v))
+        if events is not None:
+            events[0].record()
+        check(lib().dt_flash_fwd_bf16_exchange(qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), self._fused[2][buf],
+                                               self.world, self.rank, M // self.world, None, None, B, T, Hl, D,
+                                               float(scale), int(bool(causal)),
+                                               torch.cuda.current_stream(q.device).cuda_stream))
+        if events is not None:
+            events[1].record()
+        # stream-ordered barrier: every rank's stores into my buffer precede my projection
+        dist.all_reduce(self._barrier, group=self.group)
+        return self._fused[1][buf]
+
     def forward(self, q, k, v, scale: float, causal: bool = True, events=None) -> torch.Tensor:
         B, T, Hl, D = q.shape
         if Hl != self.h1 - self.h0 or D != self.head_dim:
             raise ValueError(f"expected [B, T, {self.h1 - self.h0}, {self.head_dim}] local heads")
         token_range(self.rank, self.world, B * T)  # validates divisibility
-        o_local = self.local_attention(q, k, v, scale, causal, events)
-        a = self.exchange(o_local)
+        if self.world > 1 and self.exchange_mode == "fused" and q.is_cuda:
+            a = self.fused_attention_exchange(q, k, v, scale, causal, events)
+        else:
+            o_local = self.local_attention(q, k, v, scale, causal, events)
+            a = self.exchange(o_local)
         return self.project(a, self.world)
 
     __call__ = forward

@@ -87,6 +87,27 @@ int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int 
                       float* softmax_m, float* softmax_l, const int* seq_lens, int B, int T, int H, int D,
                       float scale, int causal, void* stream);
 
+/* Flash attention fused with the head-parallel exchange (the head-sharded
+ * form of flash_attention_forward + the reshape feeding OlmoAttention.cpp:99-107):
+ * this rank (`rank` of `ranks`, <= 8) holds H heads of q, k, v (bf16
+ * [B, T, H, D]); each output row of global token g = b*T + t is stored, bf16,
+ * straight into recv_bufs[g / tokens_per_rank] -- this GPU's own receive buffer
+ * or a peer's, mapped with dt_ipc_open -- at plane `rank`, row
+ * g % tokens_per_rank.  A receive buffer is [ranks][tokens_per_rank][H*D]
+ * bf16, the planar A operand of dt_gemm_bf16_tn_planar.  The caller orders the
+ * owners' reads after every rank's kernel (e.g. a one-element all-reduce on the
+ * same stream) and double-buffers the receive buffers across steps. */
+int dt_flash_fwd_bf16_exchange(const void* q, const void* k, const void* v, void* const* recv_bufs, int ranks,
+                               int rank, long long tokens_per_rank, float* softmax_m, float* softmax_l, int B, int T,
+                               int H, int D, float scale, int causal, void* stream);
+/* CUDA IPC for the exchange buffers.  dt_ipc_get_handle writes the 64-byte
+ * handle of the allocation holding dev_ptr and dev_ptr's offset inside it;
+ * dt_ipc_open maps a peer's handle (peer access enabled lazily) and returns the
+ * mapped base + offset; dt_ipc_close unmaps it (same pointer and offset). */
+int dt_ipc_get_handle(const void* dev_ptr, void* handle_out, size_t* offset_out);
+int dt_ipc_open(const void* handle, size_t offset, void** dev_ptr_out);
+int dt_ipc_close(void* dev_ptr, size_t offset);
+
 /* ---- attention layer ----------------------------------------------------
  * Replaces class OlmoAttention (OlmoAttention.h:10-42): constructor
  * (OlmoAttention.cpp:39-53) and forward (OlmoAttention.cpp:56-108):
@@ -119,6 +140,52 @@ int dt_attn_forward(dt_attn* attn, const float* x, int B, int T, const int* seq_
 /* Same with host buffers; seq_lens is a host int[B] or NULL. */
 int dt_attn_forward_host(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y);
 int dt_attn_destroy(dt_attn* attn);
+
+/* ---- full model prefill (configuration 3) -------------------------------
+ * Replaces OlmoModel::forward (OlmoModel.cpp:25-48) with OlmoBlock::forward
+ * (OlmoBlock.cpp:13-21), OlmoMlp::forward (OlmoMlp.cpp:26-63) and
+ * OlmoLmHead::forward (OlmoLmHead.cpp:11-28): x = embed[ids]; per layer
+ * h = x + RMSNorm(attn(x)), x = h + RMSNorm(mlp(h)); logits = RMSNorm(x) Wlm^T.
+ * The residual stream stays fp32; GEMM operands are bf16 copies. */
+typedef struct dt_model dt_model;
+
+typedef struct dt_model_layer_weights {
+    const float* q_proj; /* [d, d] */
+    const float* k_proj;
+    const float* v_proj;
+    const float* o_proj;
+    const float* q_norm; /* [d] */
+    const float* k_norm;
+    const float* post_attention_norm;   /* [d] */
+    const float* gate_proj;             /* [hidden, d] */
+    const float* up_proj;               /* [hidden, d] */
+    const float* down_proj;             /* [d, hidden] */
+    const float* post_feedforward_norm; /* [d] */
+} dt_model_layer_weights;
+
+typedef struct dt_model_weights {
+    const float* embed;      /* [vocab, d] */
+    const float* final_norm; /* [d] */
+    const float* lm_head;    /* [vocab, d] */
+    const dt_model_layer_weights* layers;
+    int n_layers;            /* 16 (model_config.h:7) */
+    int vocab;               /* 100352; multiple of 8 */
+    int d_model;             /* 2048 */
+    int n_heads;             /* 16 */
+    int hidden;              /* 8192; multiple of 128 */
+    float eps;
+    float rope_theta;
+} dt_model_weights;
+
+int dt_model_create(const dt_model_weights* w, int device, dt_model** out);
+/* Reads the checkpoint folder as OlmoModel.cpp:11-22 does (n_layers <= 0 means 16). */
+int dt_model_create_from_npy(const char* folder, int n_layers, int device, dt_model** out);
+/* tokens: uint32 [B, T] device; logits: fp32 [B, T, vocab] device.  Token ids
+ * must be below vocab (the gather clamps, it does not check). */
+int dt_model_forward(dt_model* m, const uint32_t* tokens, int B, int T, float* logits, void* stream);
+/* Host buffers; token ids are checked against the vocabulary. */
+int dt_model_forward_host(dt_model* m, const uint32_t* tokens, int B, int T, float* logits);
+int dt_model_destroy(dt_model* m);
 
 /* ---- stages (for stage-wise parity checks and head-sharded callers) ----- */
 /* dst[i] = bf16(src[i]), n elements (n % 4 == 0). */

@@ -69,6 +69,10 @@ def lib():
                                             _f64p, _f64p, _f64p]
         L.or_attention_layer.argtypes = [_f32p] * 8 + [ctypes.c_long, ctypes.c_long, ctypes.c_int, ctypes.c_int,
                                                        ctypes.c_float, ctypes.c_double] + [ctypes.c_void_p] * 4
+        L.or_mlp.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_long, ctypes.c_int, ctypes.c_int]
+        L.or_model_forward.argtypes = [ctypes.c_void_p, ctypes.c_long, ctypes.c_long, _f32p, ctypes.c_void_p,
+                                       ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_float, ctypes.c_double, _f32p]
         L.or_set_threads(0)
         _lib = L
     return _lib
@@ -190,3 +194,45 @@ def ref_flash_fwd(q, k, v, scale: float, causal: bool = True, threads: int = 0):
     if secs < 0:
         raise RuntimeError("reference flash_attention_forward raised")
     return o, m, l, secs
+
+
+class _LayerW(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm", "post_attention_norm", "gate_proj", "up_proj",
+        "down_proj", "post_feedforward_norm")]
+
+
+LAYER_KEYS = ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm", "post_attention_norm", "gate_proj",
+              "up_proj", "down_proj", "post_feedforward_norm")
+
+
+def mlp(x, w_gate, w_up, w_down):
+    """Restated OlmoMlp::forward (OlmoMlp.cpp:26-63).  x: [M, d]."""
+    x = _c(x)
+    M, d = x.shape
+    hidden = w_up.shape[0]
+    out = np.empty_like(x)
+    lib().or_mlp(x, _c(w_gate), _c(w_up), _c(w_down), out, M, d, hidden)
+    return out
+
+
+def model_forward(ids, embed, layers, final_norm, lm_head, n_heads: int = 16, eps: float = 1e-6,
+                  theta: float = 500000.0):
+    """Restated OlmoModel::forward (OlmoModel.cpp:25-48).  ids: [B, T] uint32;
+    layers: list of dicts with LAYER_KEYS.  Returns logits [B, T, vocab]."""
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    B, T = ids.shape
+    embed = _c(embed)
+    vocab, d = embed.shape
+    hidden = layers[0]["up_proj"].shape[0]
+    keep = []
+    arr = (_LayerW * len(layers))()
+    for i, lw in enumerate(layers):
+        for k in LAYER_KEYS:
+            a = _c(lw[k])
+            keep.append(a)
+            setattr(arr[i], k, a.ctypes.data)
+    logits = np.empty((B, T, lm_head.shape[0]), np.float32)
+    lib().or_model_forward(ids.ctypes.data, B, T, embed, ctypes.cast(arr, ctypes.c_void_p), len(layers),
+                           _c(final_norm), _c(lm_head), lm_head.shape[0], d, n_heads, hidden, eps, theta, logits)
+    return logits

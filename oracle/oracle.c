@@ -260,3 +260,59 @@ void or_attention_layer(const float* x, const float* wq, const float* wk, const 
     if (a_out) memcpy(a_out, a, sizeof(float) * n);
     free(p); free(q); free(k); free(v); free(a); free(st); free(ct);
 }
+
+/* SwiGLU MLP, OlmoMlp.cpp:26-63: up = x Wup^T, gate = x Wgate^T (weights
+ * [hidden, d]), act = gate / (1 + exp(-gate)) * up (:48-52), out = act Wdown^T
+ * (Wdown [d, hidden]).  x, out: [M, d]. */
+void or_mlp(const float* x, const float* w_gate, const float* w_up, const float* w_down, float* out,
+            long M, int d, int hidden) {
+    float* up = (float*)malloc(sizeof(float) * (size_t)M * hidden);
+    float* gate = (float*)malloc(sizeof(float) * (size_t)M * hidden);
+    or_linear(x, w_up, up, M, hidden, d);
+    or_linear(x, w_gate, gate, M, hidden, d);
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < M * (long)hidden; ++i) {
+        const float g = gate[i];
+        gate[i] = g / (1.0f + expf(-g)) * up[i];
+    }
+    or_linear(gate, w_down, out, M, d, hidden);
+    free(up);
+    free(gate);
+}
+
+/* Weights of one decoder layer, in the checkpoint's layouts. */
+typedef struct {
+    const float *q_proj, *k_proj, *v_proj, *o_proj, *q_norm, *k_norm;
+    const float *post_attention_norm, *gate_proj, *up_proj, *down_proj, *post_feedforward_norm;
+} or_layer_weights;
+
+/* Full model prefill, OlmoModel.cpp:25-48 with OlmoBlock.cpp:13-21:
+ * x = embed[ids]; per layer: h = x + norm_pa(attn(x)); x = h + norm_pf(mlp(h));
+ * logits = norm_final(x) Wlm^T.  ids: [B, T] uint32; logits: [B, T, vocab].
+ * n_layers and vocab are parameters (the reference fixes 16 and 100352) so
+ * tests can run reduced models; everything else follows the reference. */
+void or_model_forward(const unsigned* ids, long B, long T, const float* embed, const or_layer_weights* layers,
+                      int n_layers, const float* final_norm, const float* lm_head, int vocab, int d_model,
+                      int n_heads, int hidden, float eps, double theta, float* logits) {
+    const long M = B * T;
+    const size_t n = (size_t)M * d_model;
+    float* x = (float*)malloc(sizeof(float) * n);
+    float* y = (float*)malloc(sizeof(float) * n);
+    float* t = (float*)malloc(sizeof(float) * n);
+    for (long i = 0; i < M; ++i) memcpy(x + (size_t)i * d_model, embed + (size_t)ids[i] * d_model, sizeof(float) * d_model);
+    for (int li = 0; li < n_layers; ++li) {
+        const or_layer_weights* w = &layers[li];
+        or_attention_layer(x, w->q_proj, w->k_proj, w->v_proj, w->o_proj, w->q_norm, w->k_norm, y, B, T, d_model,
+                           n_heads, eps, theta, NULL, NULL, NULL, NULL);
+        or_rmsnorm(y, w->post_attention_norm, t, M, d_model, eps);
+        for (size_t i = 0; i < n; ++i) x[i] += t[i]; /* x is now h */
+        or_mlp(x, w->gate_proj, w->up_proj, w->down_proj, y, M, d_model, hidden);
+        or_rmsnorm(y, w->post_feedforward_norm, t, M, d_model, eps);
+        for (size_t i = 0; i < n; ++i) x[i] += t[i];
+    }
+    or_rmsnorm(x, final_norm, t, M, d_model, eps);
+    or_linear(t, lm_head, logits, M, vocab, d_model);
+    free(x);
+    free(y);
+    free(t);
+}

@@ -22,18 +22,23 @@ def _reference(B, T, H):
     return q, k, v, wo, oracle.linear(o.reshape(B * T, 2048), wo)
 
 
-def _run_rank(rank, world, q, k, v, wo):
+def _run_rank(rank, world, q, k, v, wo, exchange="fused", steps=1):
     import torch
 
     from dirktensor_b200.head_parallel import HeadParallelAttention, head_range
 
     dev = torch.device("cuda", rank)
     h0, h1 = head_range(rank, world, H)
-    hp = HeadParallelAttention(torch.from_numpy(wo).to(dev), n_heads=H, head_dim=128)
+    hp = HeadParallelAttention(torch.from_numpy(wo).to(dev), n_heads=H, head_dim=128, exchange=exchange)
     ql, kl, vl = (torch.from_numpy(np.ascontiguousarray(a[:, :, h0:h1])).to(dev) for a in (q, k, v))
-    y = hp.forward(ql, kl, vl, SCALE, True)
+    ys = []
+    for _ in range(steps):  # several steps exercise both receive buffers
+        ys.append(hp.forward(ql, kl, vl, SCALE, True).cpu().numpy())
     torch.cuda.synchronize(dev)
-    return y.cpu().numpy()
+    hp.close()
+    for y in ys[1:]:
+        assert np.array_equal(y, ys[0])
+    return ys[0]
 
 
 def test_head_parallel_world1_vs_oracle(cuda):
@@ -63,7 +68,7 @@ def test_planar_gemm_equals_plain_gemm_on_concatenated_planes(cuda):
     assert torch.equal(y, y2)
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, exchange):
     import torch
     import torch.distributed as dist
 
@@ -74,13 +79,14 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     q, k, v, wo, _ = _reference(B, T, H)
-    y = _run_rank(rank, world, q, k, v, wo)
+    y = _run_rank(rank, world, q, k, v, wo, exchange=exchange, steps=3)
     np.save(os.path.join(out_dir, f"y{rank}.npy"), y)
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_head_parallel_world2_nccl(cuda, tmp_path):
+@pytest.mark.parametrize("exchange", ["fused", "nccl"])
+def test_head_parallel_world2(cuda, tmp_path, exchange):
     import torch
     import torch.multiprocessing as mp
 
@@ -91,7 +97,7 @@ def test_head_parallel_world2_nccl(cuda, tmp_path):
     port = s.getsockname()[1]
     s.close()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), exchange)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
