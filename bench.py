@@ -200,12 +200,13 @@ def main():
     ap.add_argument("--impl", default="dirktensor", choices=["dirktensor", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="nccl", choices=["fused", "nccl"],
-                    help="N>1: NCCL all-to-all (default) or fused flash + NVLink stores")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
+                    help="N>1: fused flash + NVLink stores (default) or an NCCL all-to-all")
     ap.add_argument("--case", default=None, choices=["flash_bf16", "layer"],
                     help="profiling case for ncu: a few launches of one stage, no timing")
     ap.add_argument("--sweep", action="store_true",
                     help="config-1 sweep (T = 64 ... 6144) and config 4: flash kernel TFLOP/s per shape")
+    ap.add_argument("--no-model", action="store_true", help="skip the config-3 full-model measurement")
     ap.add_argument("--batch", type=int, default=4)
     ap.add_argument("--seq", type=int, default=4096)
     args = ap.parse_args()
@@ -315,8 +316,11 @@ def main():
         t4096 = bench_t4096(torch, dt, dev, args)
 
     layers = None
+    model3 = None
     if world == 1:
         layers = bench_layers(torch, dt, dev, args)
+        if not args.no_model:
+            model3 = bench_model(torch, dt, dev, args)
 
     # ---- CPU baseline (rank 0, N=1) ---------------------------------------
     cpu = None
@@ -366,6 +370,7 @@ def main():
             "clocks": clocks,
             "config1_t4096": t4096,
             "layers": layers,
+            "model_config3": model3,
         }
         print(json.dumps(line), flush=True)
     hp.close()
@@ -412,6 +417,56 @@ def bench_layers(torch, dt, dev, args):
     dt.check_device_error()
     attn.close()
     return out
+
+
+def bench_model(torch, dt, dev, args):
+    """Configuration 3: full 16-layer OLMo-2-0425-1B prefill, B=4, T=4096,
+    vocab 100352, random weights N(0, 0.02) (two distinct layer weight sets,
+    uploaded into 16 separate layers), token ids seeded uniform in [0, 100278).
+    FLOPs: 2 * tokens * (16 * (4 d^2 + 3 d * 8192) + 100352 d) for the
+    matmuls plus 16 * 2 * B * H * T^2 * D for causal attention."""
+    Bm, Tm, vocab, hidden, nl = 4, 4096, 100352, 8192, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+
+    def rnd(*shape, scale=0.02):
+        return (torch.randn(shape, generator=g, device=dev) * scale).cpu().numpy()
+
+    def gain():
+        return (1 + torch.randn((DM,), generator=g, device=dev) * 0.02).cpu().numpy()
+
+    base = []
+    for _ in range(2):
+        base.append({"q_proj": rnd(DM, DM), "k_proj": rnd(DM, DM), "v_proj": rnd(DM, DM), "o_proj": rnd(DM, DM),
+                     "q_norm": gain(), "k_norm": gain(), "post_attention_norm": gain(),
+                     "gate_proj": rnd(hidden, DM), "up_proj": rnd(hidden, DM), "down_proj": rnd(DM, hidden),
+                     "post_feedforward_norm": gain()})
+    layers = [base[i % 2] for i in range(nl)]
+    model = dt.OlmoModel.from_weights(rnd(vocab, DM), layers, gain(), rnd(vocab, DM), device=dev.index or 0)
+    del base, layers
+    ids = torch.randint(0, 100278, (Bm, Tm), generator=g, device=dev, dtype=torch.int32)
+    logits = torch.empty((Bm, Tm, vocab), dtype=torch.float32, device=dev)
+    for _ in range(2):
+        model.forward(ids, out=logits)
+    torch.cuda.synchronize()
+    reps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        model.forward(ids, out=logits)
+    e1.record()
+    torch.cuda.synchronize()
+    dt.check_device_error()
+    ms = e0.elapsed_time(e1) / reps
+    tokens = Bm * Tm
+    flops = 2.0 * tokens * (nl * (4 * DM * DM + 3 * DM * hidden) + vocab * DM) + nl * 2.0 * Bm * H * Tm * Tm * D
+    finite = bool(torch.isfinite(logits[0, :8]).all().item())
+    model.close()
+    del logits
+    torch.cuda.empty_cache()
+    return {"B": Bm, "T": Tm, "n_layers": nl, "vocab": vocab, "ms": ms, "tok_s": tokens / (ms * 1e-3),
+            "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "logits_finite": finite,
+            "data": "synthetic ids, random N(0,0.02) weights"}
 
 
 def bench_t4096(torch, dt, dev, args):

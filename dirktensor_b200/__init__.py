@@ -7,6 +7,7 @@ from ._lib import DTError, lib  # noqa: F401  (loads the CUDA library; raises if
 from .attention import (  # noqa: F401
     FlashAttentionResult,
     OlmoAttention,
+    OlmoModel,
     cast_bf16,
     check_device_error,
     d_model,

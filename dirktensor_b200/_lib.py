@@ -48,6 +48,28 @@ class dt_attn_weights(ctypes.Structure):
     ]
 
 
+class dt_model_layer_weights(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm", "post_attention_norm", "gate_proj", "up_proj",
+        "down_proj", "post_feedforward_norm")]
+
+
+class dt_model_weights(ctypes.Structure):
+    _fields_ = [
+        ("embed", ctypes.c_void_p),
+        ("final_norm", ctypes.c_void_p),
+        ("lm_head", ctypes.c_void_p),
+        ("layers", ctypes.POINTER(dt_model_layer_weights)),
+        ("n_layers", ctypes.c_int),
+        ("vocab", ctypes.c_int),
+        ("d_model", ctypes.c_int),
+        ("n_heads", ctypes.c_int),
+        ("hidden", ctypes.c_int),
+        ("eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+    ]
+
+
 _lib = None
 
 _P = ctypes.c_void_p
@@ -61,6 +83,7 @@ SIGNATURES = {
     "dt_last_error": (ctypes.c_char_p, []),
     "dt_version": (_I, []),
     "dt_check_device_error": (_I, []),
+    "dt_selftest_expired_wait": (_I, []),
     "dt_flash_fwd_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "dt_flash_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P, _SZ, _P]),
     "dt_flash_fwd_host": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I]),
@@ -76,6 +99,12 @@ SIGNATURES = {
     "dt_attn_forward": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "dt_attn_forward_host": (_I, [_P, _P, _I, _I, _P, _P]),
     "dt_attn_destroy": (_I, [_P]),
+    "dt_model_create": (_I, [ctypes.POINTER(dt_model_weights), _I, ctypes.POINTER(_P)]),
+    "dt_model_create_from_npy": (_I, [ctypes.c_char_p, _I, _I, ctypes.POINTER(_P)]),
+    "dt_model_forward": (_I, [_P, _P, _I, _I, _P, _P]),
+    "dt_model_forward_host": (_I, [_P, _P, _I, _I, _P]),
+    "dt_model_destroy": (_I, [_P]),
+    "dt_model_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "dt_cast_f32_bf16": (_I, [_P, _P, _LL, _P]),
     "dt_gemm_bf16_tn": (_I, [_P, _P, _P, _I, _I, _I, _I, _LL, _P]),
     "dt_gemm_bf16_tn_planar": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _LL, _P]),

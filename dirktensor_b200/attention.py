@@ -16,7 +16,7 @@ from typing import NamedTuple, Optional
 
 import numpy as np
 
-from ._lib import check, dt_attn_weights, lib
+from ._lib import check, dt_attn_weights, dt_model_layer_weights, dt_model_weights, lib
 
 # model_config.h:3-7
 head_dim = 128
@@ -250,6 +250,79 @@ class OlmoAttention:
     def close(self):
         if self._h:
             lib().dt_attn_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+LAYER_KEYS = ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm", "post_attention_norm", "gate_proj",
+              "up_proj", "down_proj", "post_feedforward_norm")
+
+
+class OlmoModel:
+    """Full OLMo-2 prefill on the GPU: mirror of OlmoModel (OlmoModel.h:11-31),
+    forward path.  ``OlmoModel(folder)`` reads the checkpoint as OlmoModel.cpp:11-22
+    does; ``OlmoModel.from_weights`` takes arrays (a list of per-layer dicts with
+    LAYER_KEYS).  ``forward(ids)`` returns logits [B, T, vocab] (fp32)."""
+
+    def __init__(self, folder: Optional[str] = None, device: int = 0, n_layers: int = n_layers, _handle=None):
+        self._h = ctypes.c_void_p()
+        self.device = device
+        if _handle is not None:
+            self._h = _handle
+        elif folder is not None:
+            check(lib().dt_model_create_from_npy(folder.encode(), int(n_layers), int(device), ctypes.byref(self._h)))
+        else:
+            raise ValueError("OlmoModel needs a checkpoint folder (or use from_weights)")
+        nl, voc, hid = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        check(lib().dt_model_info(self._h, ctypes.byref(nl), ctypes.byref(voc), ctypes.byref(hid)))
+        self.n_layers, self.vocab, self.hidden = nl.value, voc.value, hid.value
+
+    @classmethod
+    def from_weights(cls, embed, layers, final_norm, lm_head, device: int = 0, eps: float = rms_eps,
+                     theta: float = rope_theta) -> "OlmoModel":
+        embed = np.ascontiguousarray(embed, dtype=np.float32)
+        lm_head = np.ascontiguousarray(lm_head, dtype=np.float32)
+        final_norm = np.ascontiguousarray(final_norm, dtype=np.float32)
+        keep = [embed, lm_head, final_norm]
+        arr = (dt_model_layer_weights * len(layers))()
+        for i, lw in enumerate(layers):
+            for k in LAYER_KEYS:
+                a = np.ascontiguousarray(lw[k], dtype=np.float32)
+                keep.append(a)
+                setattr(arr[i], k, a.ctypes.data)
+        hidden = int(np.asarray(layers[0]["up_proj"]).shape[0])
+        w = dt_model_weights(embed.ctypes.data, final_norm.ctypes.data, lm_head.ctypes.data, arr, len(layers),
+                             int(embed.shape[0]), d_model, n_heads, hidden, eps, theta)
+        h = ctypes.c_void_p()
+        check(lib().dt_model_create(ctypes.byref(w), int(device), ctypes.byref(h)))
+        return cls(device=device, _handle=h)
+
+    def forward(self, ids, out=None):
+        """ids: [B, T] uint32/int token ids (CUDA tensor: device path; numpy: host path)."""
+        if _is_torch(ids):
+            torch = _torch()
+            B, T = ids.shape
+            t = ids.to(torch.int32).contiguous()
+            logits = out if out is not None else torch.empty((B, T, self.vocab), dtype=torch.float32,
+                                                             device=ids.device)
+            check(lib().dt_model_forward(self._h, t.data_ptr(), B, T, logits.data_ptr(), _stream_ptr(ids.device)))
+            return logits
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        B, T = ids.shape
+        logits = np.empty((B, T, self.vocab), np.float32)
+        check(lib().dt_model_forward_host(self._h, ids.ctypes.data, B, T, logits.ctypes.data))
+        return logits
+
+    __call__ = forward
+
+    def close(self):
+        if self._h:
+            lib().dt_model_destroy(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):

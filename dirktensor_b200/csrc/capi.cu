@@ -20,6 +20,20 @@
 #include "model.cuh"
 #include "prologue.cuh"
 
+namespace dt {
+// Diagnostic for the failure path: one thread waits on an mbarrier that nothing
+// arrives on.  mbar_wait gives up after its budget, records the site in the
+// device error word and the kernel returns normally.
+__global__ void expired_wait_kernel(unsigned site) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_wait(&bar, 0, site);
+    }
+}
+}  // namespace dt
+
 namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
@@ -421,6 +435,24 @@ extern "C" {
 const char* dt_last_error(void) { return t_last_error.c_str(); }
 
 int dt_version(void) { return kVersion; }
+
+int dt_selftest_expired_wait(void) {
+    t_last_error.clear();
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    DT_CUDA(cudaDeviceSynchronize());
+    bool had = false;
+    DT_TRY(read_device_error(&had));  // start from a clear word
+    dt::expired_wait_kernel<<<1, 32>>>(0x7e);
+    DT_CUDA(cudaGetLastError());
+    DT_CUDA(cudaDeviceSynchronize());
+    const int st = read_device_error(&had);
+    if (st == DT_ERR_DEVICE_TIMEOUT && had) {
+        t_last_error.clear();
+        return DT_OK;
+    }
+    return fail(DT_ERR_CUDA, "expected the wait to expire and be reported (status %d)", st);
+}
 
 int dt_check_device_error(void) {
     DT_CUDA(cudaDeviceSynchronize());
@@ -1225,6 +1257,15 @@ int dt_model_forward(dt_model* m, const uint32_t* tokens, int B, int T, float* l
                                                                           m->eps, 0);          // final norm
     DT_CUDA(cudaGetLastError());
     return launch_gemm(xb, m->lm_head, logits, 0, (int)M, m->vocab, d, m->vocab, st);           // LM head
+}
+
+int dt_model_info(const dt_model* m, int* n_layers, int* vocab, int* hidden) {
+    t_last_error.clear();
+    if (!m) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (n_layers) *n_layers = m->n_layers;
+    if (vocab) *vocab = m->vocab;
+    if (hidden) *hidden = m->hidden;
+    return DT_OK;
 }
 
 int dt_model_forward_host(dt_model* m, const uint32_t* tokens, int B, int T, float* logits) {

@@ -123,6 +123,10 @@ __device__ __forceinline__ void store_chunk(const Params& p, int b, int t, int h
     }
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -375,7 +379,56 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         const bool row_valid = q_pos < Tb;
         bool have_o = false;
         if (n > 0 && ok) have_o = mbar_wait(&sm.o_full[i], 0, kSiteO);
-        if (have_o) {
+        if (have_o && p.out_bf16) {
+            // bf16 rows leave through shared memory so that global (or peer)
+            // stores are coalesced: each warp stages its 32 rows (256 B each) in
+            // its quarter of this tile's Q buffer -- idle now, since o_full
+            // follows every S_i product that read it -- then writes two whole
+            // rows (512 contiguous bytes) per instruction.  Warp-local only.
+            tc_fence_after();
+            const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+            const float mul = row_valid ? inv_l : 0.f;
+            const uint32_t stage = smem_u32(sm.q[i]) + (uint32_t)(warp & 3) * 8192;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                float o[32];
+                tmem_ld32(tO + cc * 32, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {  // 16-byte chunk 4cc+m of this row, XOR-swizzled by row
+                    const uint32_t chunk = (uint32_t)(4 * cc + m) ^ (uint32_t)(lane & 15);
+                    st_shared_v4(stage + (uint32_t)lane * 256 + chunk * 16,
+                                 pack_bf16x2(o[8 * m + 0] * mul, o[8 * m + 1] * mul),
+                                 pack_bf16x2(o[8 * m + 2] * mul, o[8 * m + 3] * mul),
+                                 pack_bf16x2(o[8 * m + 4] * mul, o[8 * m + 5] * mul),
+                                 pack_bf16x2(o[8 * m + 6] * mul, o[8 * m + 7] * mul));
+                }
+            }
+            __syncwarp();
+#pragma unroll 4
+            for (int step = 0; step < 16; ++step) {
+                const int rr = 2 * step + (lane >> 4);            // row within this warp's 32
+                const uint32_t chunk = (uint32_t)(lane & 15);
+                const int t = qt + (warp & 3) * 32 + rr;
+                uint32_t a, bb, c2, d;
+                asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(a), "=r"(bb), "=r"(c2), "=r"(d)
+                             : "r"(stage + (uint32_t)rr * 256 + ((chunk ^ (uint32_t)(rr & 15)) << 4)));
+                if (t < p.T) {
+                    const long long g = (long long)b * p.T + t;
+                    void* dst = p.out;
+                    long long row = g;
+                    if (p.scatter_ranks > 0) {
+                        const int rk = static_cast<int>(g / p.tokens_per_rank);
+                        dst = p.scatter_dst[rk];
+                        row = (long long)p.scatter_plane * p.tokens_per_rank + (g - (long long)rk * p.tokens_per_rank);
+                    }
+                    uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + row * p.out_row_stride +
+                                                         (long long)h * kD) + chunk;
+                    *d4 = make_uint4(a, bb, c2, d);
+                }
+            }
+        } else if (have_o) {
             tc_fence_after();
             const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
 #pragma unroll

@@ -49,6 +49,13 @@ int dt_version(void);
  * The device-pointer entry points do not synchronise; call this after them. */
 int dt_check_device_error(void);
 
+/* Exercises the failure path on the current device: runs a kernel whose
+ * barrier wait can never complete; the wait's 1-second budget expires, the
+ * kernel records it and returns, and this call checks that the expiry was
+ * reported (then clears it).  DT_OK means the mechanism works and the context
+ * is still usable.  Takes about one second. */
+int dt_selftest_expired_wait(void);
+
 /* ---- flash attention forward -------------------------------------------
  * Replaces flash_attention_forward (FlashAttention.h:15-21,
  * FlashAttention.cpp:24-182) and fills FlashAttentionResult
@@ -186,6 +193,8 @@ int dt_model_forward(dt_model* m, const uint32_t* tokens, int B, int T, float* l
 /* Host buffers; token ids are checked against the vocabulary. */
 int dt_model_forward_host(dt_model* m, const uint32_t* tokens, int B, int T, float* logits);
 int dt_model_destroy(dt_model* m);
+/* Layer count, vocabulary and MLP width of a created model (any may be NULL). */
+int dt_model_info(const dt_model* m, int* n_layers, int* vocab, int* hidden);
 
 /* ---- stages (for stage-wise parity checks and head-sharded callers) ----- */
 /* dst[i] = bf16(src[i]), n elements (n % 4 == 0). */

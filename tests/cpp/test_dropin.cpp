@@ -6,6 +6,8 @@
 //   test_dropin flash <dir> B T H     reads dir/{q,k,v}.f32, writes dir/{o,m,l}.f32
 //   test_dropin layer <dir> index B T reads dir/x.f32 and the layer's .npy weights
 //                                     from dir, writes dir/y.f32
+//   test_dropin model <dir> L B T     reads dir/ids.u32 and an L-layer checkpoint from
+//                                     dir, writes dir/logits.f32 (OlmoModel)
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -15,6 +17,7 @@
 
 #include "FlashAttention.h"
 #include "OlmoAttention.h"
+#include "OlmoModel.h"
 
 template <class X>
 static void read_into(const std::string& path, X& x) {
@@ -66,6 +69,20 @@ int main(int argc, char** argv) {
             const xt::xtensor<float, 3> y = moved.forward(x);
             write_from(dir + "/y.f32", y);
             moved.m_attention.zero_grad();
+        } else if (mode == "model" && argc == 6) {
+            const unsigned layers = static_cast<unsigned>(std::stoul(argv[3]));
+            const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);
+            xt::xtensor<uint32_t, 2> ids = xt::empty<uint32_t>({B, T});
+            std::ifstream f(dir + "/ids.u32", std::ios::binary);
+            f.read(reinterpret_cast<char*>(ids.data()), static_cast<std::streamsize>(ids.size() * 4));
+            OlmoModel model(dir, layers);
+            const xt::xtensor<float, 3> logits = model.forward(ids);
+            write_from(dir + "/logits.f32", logits);
+            try {
+                model.step(1e-4f);
+                return 3;
+            } catch (const std::logic_error&) {
+            }
         } else {
             throw std::runtime_error("bad arguments");
         }

@@ -53,3 +53,24 @@ def test_dropin_olmo_attention_block_usage(cuda, dropin_bin, tmp_path):
     # a missing layer surfaces as a C++ exception -> non-zero exit
     r = subprocess.run([dropin_bin, "layer", str(tmp_path), "6", str(B), str(T)], capture_output=True, text=True)
     assert r.returncode == 1 and "cannot open" in r.stderr
+
+
+def test_dropin_olmo_model(cuda, dropin_bin, tmp_path):
+    """OlmoModel(folder).forward(batch) -> logits, as test_olmo_model.cpp:24-45 calls it."""
+    from test_model_gpu import KEYS, model_weights
+
+    embed, layers, final_norm, lm_head = model_weights(9, 2, 512)
+    np.save(tmp_path / "model.embed_tokens.weight.npy", embed)
+    np.save(tmp_path / "model.norm.weight.npy", final_norm)
+    np.save(tmp_path / "lm_head.weight.npy", lm_head)
+    names = {"post_attention_norm": "post_attention_layernorm", "post_feedforward_norm": "post_feedforward_layernorm",
+             "gate_proj": "mlp.gate_proj", "up_proj": "mlp.up_proj", "down_proj": "mlp.down_proj"}
+    for i, lw in enumerate(layers):
+        for k in KEYS:
+            np.save(tmp_path / f"model.layers.{i}.{names.get(k, 'self_attn.' + k)}.weight.npy", lw[k])
+    ids = np.random.default_rng(4).integers(0, 512, (2, 48)).astype(np.uint32)
+    ids.tofile(tmp_path / "ids.u32")
+    subprocess.run([dropin_bin, "model", str(tmp_path), "2", "2", "48"], check=True)
+    got = np.fromfile(tmp_path / "logits.f32", np.float32).reshape(2, 48, 512)
+    ref = oracle.model_forward(ids, embed, layers, final_norm, lm_head)
+    assert rel_l2(got, ref) < 3e-2
