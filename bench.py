@@ -202,12 +202,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1: fused flash + NVLink stores (default) or an NCCL all-to-all")
-    ap.add_argument("--case", default=None, choices=["flash_bf16", "layer"],
+    ap.add_argument("--case", default=None, choices=["flash_bf16", "layer", "gemm"],
                     help="profiling case for ncu: a few launches of one stage, no timing")
     ap.add_argument("--sweep", action="store_true",
                     help="config-1 sweep (T = 64 ... 6144) and config 4: flash kernel TFLOP/s per shape")
     ap.add_argument("--no-model", action="store_true", help="skip the config-3 full-model measurement")
     ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--gemm-mnk", default="16384,16384,2048", help="--case gemm: M,N,K")
     ap.add_argument("--seq", type=int, default=4096)
     args = ap.parse_args()
     rank = env_int("RANK", 0)
@@ -551,8 +552,62 @@ def run_sweep(args):
                      "tflops_with_cast": f / (ms_flash + ms_cast) / 1e9})
         del q, k, v, out, qb, kb, vb
     dt.check_device_error()
+    # projection GEMMs at the configuration-3 shapes (M = 4 x 4096 tokens)
+    grows = []
+    for name, M, N, K in [("qkv", 16384, 6144, 2048), ("o_proj", 16384, 2048, 2048), ("mlp_gate_up", 16384, 16384, 2048),
+                          ("mlp_down", 16384, 2048, 8192), ("lm_head", 16384, 100352, 2048),
+                          ("config0_qkv", 512, 6144, 2048), ("config4_o_proj", 98304, 2048, 2048)]:
+        a = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        b = torch.randn((N, K), generator=g, device=dev).to(torch.bfloat16)
+        c = torch.empty((M, N), dtype=torch.float32, device=dev)
+        reps = 5
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            torch.cuda._sleep(2_000_000)
+            e = ev[i - args.warmup] if i >= args.warmup else None
+            if e:
+                e[0].record()
+            dt.gemm_bf16_tn(a, b, out=c)
+            if e:
+                e[1].record()
+        torch.cuda.synchronize()
+        ms = statistics.median(x.elapsed_time(y) for x, y in ev)
+        f = 2.0 * M * N * K
+        grows.append({"gemm": name, "M": M, "N": N, "K": K, "ms": ms, "tflops": f / ms / 1e9,
+                      "frac": f / ms / 1e9 / peak})
+        del a, b, c
+    dt.check_device_error()
+    # HBM-bound kernels: the QK-norm/RoPE prologue and the fp32->bf16 cast at the
+    # configuration-3 token count; algorithmic bytes = bytes read + bytes written once
+    hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    erows = []
+    Mt = 16384
+    qkv = torch.randn((Mt, 3 * DM), generator=g, device=dev)
+    gq = torch.ones(DM, device=dev)
+    reps = 10
+    for name in ("qk_norm_rope", "cast_f32_bf16"):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            torch.cuda._sleep(2_000_000)
+            e = ev[i - args.warmup] if i >= args.warmup else None
+            if e:
+                e[0].record()
+            if name == "qk_norm_rope":
+                dt.qk_norm_rope(qkv[:, :DM], qkv[:, DM:2 * DM], qkv[:, 2 * DM:], gq, gq, 4, 4096)
+            else:
+                dt.cast_bf16(qkv)
+            if e:
+                e[1].record()
+        torch.cuda.synchronize()
+        ms = statistics.median(x.elapsed_time(y) for x, y in ev)
+        nbytes = Mt * 3 * DM * (4 + 2)  # both kernels read 3*d fp32 and write 3*d bf16 per token
+        erows.append({"kernel": name, "tokens": Mt, "ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                      "frac_hbm": nbytes / ms / 1e6 / hbm})
+    dt.check_device_error()
     print(json.dumps({"sweep": "flash_fwd causal, H=16, D=128", "peak": peak, "peak_source": f"{src} bf16 burst",
-                      "rows": rows}), flush=True)
+                      "rows": rows, "gemm": grows, "hbm_peak_gbs": hbm, "elementwise": erows}), flush=True)
 
 
 def run_case(args):
@@ -565,7 +620,14 @@ def run_case(args):
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     Bc, Tc = args.batch, args.seq
-    if args.case == "flash_bf16":
+    if args.case == "gemm":
+        M, N, K = (int(v) for v in args.gemm_mnk.split(","))
+        a = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        b = torch.randn((N, K), generator=g, device=dev).to(torch.bfloat16)
+        c = torch.empty((M, N), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            dt.gemm_bf16_tn(a, b, out=c)
+    elif args.case == "flash_bf16":
         q, k, v = (torch.randn((Bc, Tc, H, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
         out = torch.empty((Bc, Tc, H, D), device=dev)
         for _ in range(3):

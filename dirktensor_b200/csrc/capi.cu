@@ -17,6 +17,7 @@
 #include "dt_common.cuh"
 #include "flash_fwd.cuh"
 #include "gemm.cuh"
+#include "gemm2sm.cuh"
 #include "model.cuh"
 #include "prologue.cuh"
 
@@ -152,7 +153,15 @@ std::mutex g_mu;
 DevState g_dev[64];
 
 constexpr size_t kFlashSmem = sizeof(dt::flash::Smem) + 1024;
-constexpr size_t kGemmSmem = sizeof(dt::gemm::Smem) + 1024;
+constexpr size_t kGemmSmem = sizeof(dt::gemm::SmemT<dt::gemm::kBN>) + 1024;
+constexpr size_t kGemmNarrowSmem = sizeof(dt::gemm::SmemT<dt::gemm::kNarrowBN>) + 1024;
+constexpr size_t kGemm2Smem = sizeof(dt::gemm2::Smem) + 1024;
+// GEMMs with at least this many rows run on SM pairs (gemm2sm.cuh); measured on
+// B200 at the model's shapes the pair kernel is 18-57 % faster than the one-SM
+// kernel, which remains for row counts below one pair tile's half.
+#ifndef DT_GEMM_2SM_MIN_M
+#define DT_GEMM_2SM_MIN_M 256
+#endif
 
 int current_device(int* dev) {
     DT_CUDA(cudaGetDevice(dev));
@@ -172,8 +181,12 @@ int ensure_attrs(int dev) {
     s.num_sms = prop.multiProcessorCount;
     DT_CUDA(cudaFuncSetAttribute(dt::flash::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kFlashSmem));
-    DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kGemmSmem));
+    DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kBN>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+    DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kNarrowBN>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmNarrowSmem));
+    DT_CUDA(cudaFuncSetAttribute(dt::gemm2::gemm_bf16_tn_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kGemm2Smem));
     s.attrs = true;
     return DT_OK;
 }
@@ -335,14 +348,29 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     return DT_OK;
 }
 
+// seq_lens/seq_T (optional): right-padded batch; output tiles entirely in a
+// sequence's padding are skipped (and written as zeros when pad_zero).
 int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N, int K, long long ldc,
-                cudaStream_t st, int a_planes = 1, int epilogue = dt::gemm::kStore) {
+                cudaStream_t st, int a_planes = 1, int epilogue = dt::gemm::kStore, const int* seq_lens = nullptr,
+                int seq_T = 0, int pad_zero = 0) {
     if (M == 0 || N == 0) return DT_OK;
     CUtensorMap ma, mb;
     const int plane_k = K / a_planes;
+    int dev0 = 0;
+    cudaGetDevice(&dev0);
+    const int nsm = (dev0 >= 0 && dev0 < 64) ? g_dev[dev0].num_sms : 148;
+    // Tile choice: 256 x 256 tiles on SM pairs when they fill at least every
+    // pair; otherwise 128 x 256 tiles on single SMs, narrowed to 128 x 128 when
+    // the wide tiles would leave SMs idle (the SwiGLU epilogue needs 256 columns).
+    const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    const long long wide_tiles = (long long)((M + 127) / 128) * ((N + 255) / 256);
+    const bool pair = M >= DT_GEMM_2SM_MIN_M && pair_tiles >= nsm / 2;
+    const bool narrow = !pair && epilogue == dt::gemm::kStore && wide_tiles < nsm;
+    const int bn = narrow ? dt::gemm::kNarrowBN : dt::gemm::kBN;
+    // boxes: 128 rows of A and bn rows of B per CTA, or 128 and 128 on SM pairs
     if (a_planes > 1) DT_TRY(make_map_planar(&ma, A, M, plane_k, a_planes));
     else DT_TRY(make_map_2d(&ma, A, M, K, dt::gemm::kBM));
-    DT_TRY(make_map_2d(&mb, Bm, N, K, dt::gemm::kBN));
+    DT_TRY(make_map_2d(&mb, Bm, N, K, pair ? dt::gemm2::kHalf : bn));
     dt::gemm::Params p{};
     p.M = M;
     p.N = N;
@@ -352,15 +380,34 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     p.c_bf16 = c_bf16;
     p.a_plane_k = a_planes > 1 ? plane_k : 0;
     p.epilogue = epilogue;
-    p.tiles_n = (N + dt::gemm::kBN - 1) / dt::gemm::kBN;
+    // tiles are 256 rows on SM pairs, 128 on one SM: skip only if they never straddle sequences
+    const int tile_rows = pair ? dt::gemm2::kBM : dt::gemm::kBM;
+    if (seq_lens && seq_T > 0 && (seq_T % tile_rows) == 0) {
+        p.seq_lens = seq_lens;
+        p.seq_T = seq_T;
+        p.pad_zero = pad_zero;
+    }
+    p.tiles_n = (N + bn - 1) / bn;
     const long long tiles = (long long)p.tiles_n * ((M + dt::gemm::kBM - 1) / dt::gemm::kBM);
     if (tiles > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "GEMM too large");
     p.num_tiles = (int)tiles;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
+    if (pair) {
+        // cluster tiles of 256 x 256 on SM pairs; persistent: one CTA per SM
+        p.tiles_n = (N + dt::gemm2::kBN - 1) / dt::gemm2::kBN;
+        p.num_tiles = p.tiles_n * ((M + dt::gemm2::kBM - 1) / dt::gemm2::kBM);
+        const int clusters = std::max(1, std::min(p.num_tiles, sms / 2));
+        dt::gemm2::gemm_bf16_tn_2sm_kernel<<<2 * clusters, dt::gemm2::kThreads, kGemm2Smem, st>>>(ma, mb, p);
+        DT_CUDA(cudaGetLastError());
+        return DT_OK;
+    }
     const int grid = (int)std::min<long long>(tiles, sms);  // persistent: one CTA per SM
-    dt::gemm::gemm_bf16_tn_kernel<<<grid, dt::gemm::kThreads, kGemmSmem, st>>>(ma, mb, p);
+    if (narrow)
+        dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kNarrowBN><<<grid, dt::gemm::kThreads, kGemmNarrowSmem, st>>>(ma, mb, p);
+    else
+        dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kBN><<<grid, dt::gemm::kThreads, kGemmSmem, st>>>(ma, mb, p);
     DT_CUDA(cudaGetLastError());
     return DT_OK;
 }
@@ -918,6 +965,9 @@ static size_t attn_core_bytes(long long M) { return align256(M * 6144 * 4) + 4 *
 // GEMM, QK-norm + RoPE prologue, flash attention, O projection into y (fp32).
 static int attn_core(dt_attn* a, const void* xb, int B, int T, const int* seq_lens, float* y, uint8_t* ws, int dev,
                      cudaStream_t st) {
+    // With seq_lens, projection tiles made only of padding rows are skipped: the
+    // QKV rows there are never read (attention stops at each sequence's length)
+    // and the O projection writes zeros for them.
     const long long M = (long long)B * T;
     const int d = a->d_model;
     const size_t act = align256(M * d * 2);
@@ -929,12 +979,14 @@ static int attn_core(dt_attn* a, const void* xb, int B, int T, const int* seq_le
     void* ab = rest + 3 * act;
     const float *sin_t, *cos_t;
     DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
-    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st));         // [q|k|v] = x Wqkv^T
+    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st, 1, dt::gemm::kStore, seq_lens, T,
+                       0));                                                         // [q|k|v] = x Wqkv^T
     DT_TRY(launch_prologue(qkv, qkv + d, qkv + 2 * d, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
                            st));                                                    // norm + RoPE
     DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, nullptr, nullptr, seq_lens, B, T, a->n_heads,
                         1.0f / std::sqrt(128.0f), 1, st));                          // attention
-    DT_TRY(launch_gemm(ab, a->wo, y, 0, (int)M, d, d, d, st));                     // y = a Wo^T
+    DT_TRY(launch_gemm(ab, a->wo, y, 0, (int)M, d, d, d, st, 1, dt::gemm::kStore, seq_lens, T,
+                       1));                                                         // y = a Wo^T
     return DT_OK;
 }
 

@@ -32,13 +32,18 @@ namespace dt {
 namespace gemm {
 
 constexpr int kBM = 128;
-constexpr int kBN = 256;
+constexpr int kBN = 256;                // default tile width; kNarrowBN for few-tile problems
+constexpr int kNarrowBN = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
 constexpr int kThreads = 192;
-constexpr int kAccs = 2;                // TMEM accumulators (2 x 256 columns)
+constexpr int kAccs = 2;                // TMEM accumulators (2 x BN columns)
+// stages that fit with a 128 x BN tile: 4 x 48 KB (BN 256) or 6 x 32 KB (BN 128)
+template <int BN>
+struct Cfg {
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kBBytes = BN * kBK * 2;
+};
 
 struct Params {
     int M, N, K;
@@ -49,13 +54,29 @@ struct Params {
     int tiles_n;        // ceil(N / kBN)
     int num_tiles;      // tiles_m * tiles_n
     int epilogue;       // kStore or kSwiGLU
+    // Right-padded batches (optional): rows are (sequence, position) with
+    // seq_T positions per sequence; a tile whose rows all lie at positions
+    // >= seq_lens[sequence] is padding and is skipped (zeros are written when
+    // pad_zero is set).  Only used when tiles never straddle two sequences.
+    const int* seq_lens;
+    int seq_T;
+    int pad_zero;
 };
+
+// True when rows [m0, m0 + rows) all lie in one sequence's right padding.
+__device__ __forceinline__ bool tile_is_padding(const Params& p, int m0) {
+    if (!p.seq_lens) return false;
+    const int b = m0 / p.seq_T;
+    return (m0 - b * p.seq_T) >= p.seq_lens[b];
+}
 
 enum Epilogue : int { kStore = 0, kSwiGLU = 1 };
 
-struct __align__(1024) Smem {
+template <int BN>
+struct __align__(1024) SmemT {
+    static constexpr int kStages = Cfg<BN>::kStages;
     uint8_t a[kStages][kABytes];
-    uint8_t b[kStages][kBBytes];
+    uint8_t b[kStages][Cfg<BN>::kBBytes];
     uint64_t full[kStages];
     uint64_t empty[kStages];
     uint64_t acc_full[kAccs];
@@ -63,6 +84,7 @@ struct __align__(1024) Smem {
     uint64_t mma_done;
     uint32_t tmem_base;
 };
+using Smem = SmemT<kBN>;
 
 enum : unsigned { kSiteEmpty = 0x21, kSiteFull, kSiteAcc, kSiteDone, kSiteAccEmpty };
 
@@ -98,11 +120,14 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, c
     }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const Params p) {
+    constexpr int kStages = Cfg<BN>::kStages;
+    constexpr int kBBytes = Cfg<BN>::kBBytes;
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    SmemT<BN>& sm = *reinterpret_cast<SmemT<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int nk = (p.K + kBK - 1) / kBK;
@@ -120,7 +145,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(&sm.tmem_base, kAccs * kBN);
+        tmem_alloc(&sm.tmem_base, kAccs * BN);
         tmem_relinquish();
     }
     if (warp == 0 && lane == 0) {
@@ -139,7 +164,8 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
                 const int m0 = (t / p.tiles_n) * kBM;
-                const int n0 = (t % p.tiles_n) * kBN;
+                const int n0 = (t % p.tiles_n) * BN;
+                if (tile_is_padding(p, m0)) continue;
                 for (int kb = 0; kb < nk; ++kb, ++kit) {
                     const int s = kit % kStages;
                     if (!mbar_wait(&sm.empty[s], ((kit / kStages) & 1) ^ 1, kSiteEmpty)) { ok = false; break; }
@@ -160,15 +186,18 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     } else if (warp == 1) {
         // ------------------------------ MMA issuer --------------------------
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(kBM, kBN, 0, 0);
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, 0, 0);
             int kit = 0, it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++it) {
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+                if (tile_is_padding(p, (t / p.tiles_n) * kBM)) continue;
                 const int acc = it & 1;
+                const uint32_t empty_phase = ((it >> 1) & 1) ^ 1;
+                ++it;
                 // the epilogue must have drained this accumulator (used two tiles ago)
-                if (!mbar_wait(&sm.acc_empty[acc], ((it >> 1) & 1) ^ 1, kSiteAccEmpty)) { ok = false; break; }
+                if (!mbar_wait(&sm.acc_empty[acc], empty_phase, kSiteAccEmpty)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d = tmem + acc * kBN;
+                const uint32_t d = tmem + acc * BN;
                 for (int kb = 0; kb < nk; ++kb, ++kit) {
                     const int s = kit % kStages;
                     if (!mbar_wait(&sm.full[s], (kit / kStages) & 1, kSiteFull)) { ok = false; break; }
@@ -192,20 +221,32 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         const int q = warp & 3;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int it = 0;
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
-            const int acc = it & 1;
-            if (!mbar_wait(&sm.acc_full[acc], (it >> 1) & 1, kSiteAcc)) break;
-            tc_fence_after();
+        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
             const int row = (t / p.tiles_n) * kBM + q * 32 + lane;
-            const int n0 = (t % p.tiles_n) * kBN;
-            const uint32_t taddr = tmem + lane_off + acc * kBN;
-            if (p.epilogue == kSwiGLU) {
-                const int oc0 = (t % p.tiles_n) * (kBN / 2);
+            const int n0 = (t % p.tiles_n) * BN;
+            if (tile_is_padding(p, (t / p.tiles_n) * kBM)) {
+                if (p.pad_zero && p.epilogue == kStore) {
+                    float z[32];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) z[e] = 0.f;
 #pragma unroll 1
-                for (int cc = 0; cc < kBN / 64; ++cc) {
+                    for (int cc = 0; cc < BN / 32; ++cc) store_chunk(p, row, n0 + cc * 32, z);
+                }
+                continue;
+            }
+            const int acc = it & 1;
+            const uint32_t acc_phase = (it >> 1) & 1;
+            ++it;
+            if (!mbar_wait(&sm.acc_full[acc], acc_phase, kSiteAcc)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem + lane_off + acc * BN;
+            if (p.epilogue == kSwiGLU) {
+                const int oc0 = (t % p.tiles_n) * (BN / 2);
+#pragma unroll 1
+                for (int cc = 0; cc < BN / 64; ++cc) {
                     float g[32], u[32];
                     tmem_ld32(taddr + cc * 32, g);
-                    tmem_ld32(taddr + kBN / 2 + cc * 32, u);
+                    tmem_ld32(taddr + BN / 2 + cc * 32, u);
                     tmem_wait_ld();
                     const int oc = oc0 + cc * 32;
                     if (row < p.M && oc + 32 <= p.N / 2) {
@@ -230,7 +271,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                 }
             } else {
 #pragma unroll 1
-                for (int cc = 0; cc < kBN / 32; ++cc) {
+                for (int cc = 0; cc < BN / 32; ++cc) {
                     float v[32];
                     tmem_ld32(taddr + cc * 32, v);
                     tmem_wait_ld();
@@ -248,7 +289,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kAccs * kBN);
+        tmem_dealloc(tmem, kAccs * BN);
     }
 }
 

@@ -10,7 +10,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 300, 136), (512, 6144, 2048), (1000, 2048, 2048),
-                                   (1, 40, 8)])
+                                   (1, 40, 8), (4096, 2304, 1024), (3000, 520, 8192), (200, 20000, 64)])
 def test_gemm_vs_torch_fp32(cuda, M, N, K):
     import torch
 
