@@ -78,15 +78,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `hint_ns` elapse, instead of re-polling.  A waiting warp
+// then takes no issue slots from the warps that share its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait-time hint of the sleeping wait (mbar_wait_sleep), in ns.
+#ifndef DT_WAIT_HINT_NS
+#define DT_WAIT_HINT_NS 20000
+#endif
+
 // Bounded wait: returns false (after recording `site`) if the phase with the
 // given parity does not complete within kWaitBudgetNs, or if another wait in
-// the grid already gave up.
+// the grid already gave up.  kSleep: suspend between polls (for warps that
+// share an SM sub-partition with busy warps, as in the attention kernel);
+// otherwise poll (for pipelines whose waiting warps have nothing to yield to).
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0u) {
+        const bool done = kSleep ? mbar_try_wait_sleep(bar, parity, DT_WAIT_HINT_NS) : mbar_try_wait(bar, parity);
+        if (done) return true;
+        if ((it & (kSleep ? 15u : 255u)) == 0u) {
             if (error_raised()) return false;
             if (globaltimer_ns() - t0 > kWaitBudgetNs) {
                 report_error(kDevTimeoutBase | site, parity);
@@ -94,6 +118,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
             }
         }
     }
+}
+
+// The attention kernel's wait: sleeps between polls.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, unsigned site) {
+    return mbar_wait<true>(bar, parity, site);
 }
 
 // ---------------------------------------------------------------------------
@@ -296,6 +325,13 @@ __device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, fl
     f2_unpack(t, t0, t1);
     y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
     y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32).  It
+// has no timeout: callers keep the sequence of named barriers identical on
+// every participating warp, error paths included.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Per-warpgroup register re-allocation (all 4 warps of a warpgroup execute it).

@@ -197,7 +197,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             for (int L = 0; L < 2 * nkv; ++L) {
                 const int s = L % kStages;
                 const uint32_t ph = (L / kStages) & 1;
-                if (!mbar_wait(&sm.kv_empty[s], ph ^ 1, kSiteKvEmpty)) break;
+                if (!mbar_wait_sleep(&sm.kv_empty[s], ph ^ 1, kSiteKvEmpty)) break;
                 mbar_arrive_expect_tx(&sm.kv_full[s], kTileBytes);
                 const int kt = (L >> 1) * kBN;
                 for (int hf = 0; hf < 2; ++hf) {
@@ -209,8 +209,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             if (error_raised()) {
                 // Drain copies still in flight before the CTA exits.
                 for (int L = max(0, issued - kStages); L < issued; ++L)
-                    mbar_wait(&sm.kv_full[L % kStages], (L / kStages) & 1, kSiteKvFull);
-                mbar_wait(&sm.q_full, 0, kSiteQ);
+                    mbar_wait_sleep(&sm.kv_full[L % kStages], (L / kStages) & 1, kSiteKvFull);
+                mbar_wait_sleep(&sm.q_full, 0, kSiteQ);
             }
         }
     } else if (warp == 9) {
@@ -218,7 +218,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         if (lane == 0 && nkv > 0) {
             constexpr uint32_t idesc_qk = umma_idesc_bf16(kBM, kBN, 0, 0);
             constexpr uint32_t idesc_pv = umma_idesc_bf16(kBM, kD, 0, 1);
-            bool ok = mbar_wait(&sm.q_full, 0, kSiteQ);
+            bool ok = mbar_wait_sleep(&sm.q_full, 0, kSiteQ);
             auto stage_of = [](int L) { return L % kStages; };
             auto phase_of = [](int L) { return (uint32_t)((L / kStages) & 1); };
             auto issue_s = [&](int i, int L) {
@@ -243,7 +243,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
                             (acc || kk > 0) ? 1u : 0u);
                 }
             };
-            if (ok) ok = mbar_wait(&sm.kv_full[stage_of(0)], phase_of(0), kSiteKvFull);
+            if (ok) ok = mbar_wait_sleep(&sm.kv_full[stage_of(0)], phase_of(0), kSiteKvFull);
             if (ok) {
                 tc_fence_after();
                 if (n_t0 > 0) issue_s(0, 0);
@@ -253,14 +253,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             for (int j = 0; ok && j < nkv; ++j) {
                 const int LV = 2 * j + 1, LK = 2 * j + 2;
                 const bool next_k = (j + 1) < nkv;
-                ok = mbar_wait(&sm.kv_full[stage_of(LV)], phase_of(LV), kSiteKvFull);
-                if (ok && next_k) ok = mbar_wait(&sm.kv_full[stage_of(LK)], phase_of(LK), kSiteKvFull);
+                ok = mbar_wait_sleep(&sm.kv_full[stage_of(LV)], phase_of(LV), kSiteKvFull);
+                if (ok && next_k) ok = mbar_wait_sleep(&sm.kv_full[stage_of(LK)], phase_of(LK), kSiteKvFull);
                 if (!ok) break;
                 tc_fence_after();
                 for (int i = 0; i < kQTiles; ++i) {
                     const int ni = (i == 0) ? n_t0 : n_t1;
                     if (j >= ni) continue;
-                    if (!mbar_wait(&sm.p_full[i], j & 1, kSiteP)) { ok = false; break; }
+                    if (!mbar_wait_sleep(&sm.p_full[i], j & 1, kSiteP)) { ok = false; break; }
                     tc_fence_after();
                     issue_pv(i, LV, j > 0);
                     if (j + 1 < ni) issue_s(i, LK);
@@ -272,7 +272,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             }
             // All issued tcgen05 work must be complete before TMEM is released.
             umma_commit(&sm.mma_done);
-            mbar_wait(&sm.mma_done, 0, kSiteDone);
+            mbar_wait_sleep(&sm.mma_done, 0, kSiteDone);
         }
         __syncwarp();
     } else if (warp < 8) {
@@ -288,7 +288,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         float m_run = -INFINITY, l_run = 0.f, mx = -INFINITY;
         bool ok = true;
         for (int j = 0; j < n; ++j) {
-            if (!mbar_wait(&sm.s_full[i], j & 1, kSiteS)) { ok = false; break; }
+            if (!mbar_wait_sleep(&sm.s_full[i], j & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
             float s[128];
             tmem_ld32(tS + 0, *reinterpret_cast<float(*)[32]>(s + 0));
@@ -378,7 +378,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         const bool row_in = q_pos < p.T;
         const bool row_valid = q_pos < Tb;
         bool have_o = false;
-        if (n > 0 && ok) have_o = mbar_wait(&sm.o_full[i], 0, kSiteO);
+        if (n > 0 && ok) have_o = mbar_wait_sleep(&sm.o_full[i], 0, kSiteO);
         if (have_o && p.out_bf16) {
             // bf16 rows leave through shared memory so that global (or peer)
             // stores are coalesced: each warp stages its 32 rows (256 B each) in
