@@ -4,7 +4,8 @@ ctypes bindings for
   * ``liboracle.so``: the C restatement of DirkTensor's attention hot path
     (``oracle.c``; every function there cites the reference file:line it follows);
   * ``_ref/libref_flash_<arch>.so``: the reference's own ``flash_attention_forward``
-    (FlashAttention.cpp:24-182) compiled in place against ``oracle/shims``.
+    and ``flash_attention_backward`` (FlashAttention.cpp:24-359) compiled in place
+    against ``oracle/shims``.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline legs
 may import this module.  The product (``dirktensor_b200``) never does.
@@ -73,6 +74,14 @@ def lib():
         L.or_model_forward.argtypes = [ctypes.c_void_p, ctypes.c_long, ctypes.c_long, _f32p, ctypes.c_void_p,
                                        ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_float, ctypes.c_double, _f32p]
+        L.or_sgemm.argtypes = [ctypes.c_int] * 5 + [ctypes.c_float, _f32p, ctypes.c_int, _f32p, ctypes.c_int,
+                                                     ctypes.c_float, _f32p, ctypes.c_int]
+        L.or_rmsnorm_rms.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_long, ctypes.c_int, ctypes.c_float]
+        L.or_rmsnorm_bwd.argtypes = [_f32p] * 6 + [ctypes.c_long, ctypes.c_int]
+        L.or_rope_bwd.argtypes = [_f32p, _f32p, ctypes.c_long, ctypes.c_long, ctypes.c_int, ctypes.c_int, _f32p,
+                                  _f32p]
+        L.or_flash_bwd.argtypes = [_f32p] * 10 + [ctypes.c_long, ctypes.c_long, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_float, ctypes.c_int]
         L.or_set_threads(0)
         _lib = L
     return _lib
@@ -92,6 +101,8 @@ def ref_lib():
         L.ref_flash_forward.restype = ctypes.c_double
         L.ref_flash_forward.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_long, ctypes.c_long,
                                         ctypes.c_long, ctypes.c_long, ctypes.c_float, ctypes.c_int]
+        L.ref_flash_backward.restype = ctypes.c_double
+        L.ref_flash_backward.argtypes = [_f32p] * 10 + [ctypes.c_long] * 4 + [ctypes.c_float, ctypes.c_int]
         L.arch = arch
         _ref = L
     return _ref
@@ -236,3 +247,127 @@ def model_forward(ids, embed, layers, final_norm, lm_head, n_heads: int = 16, ep
     lib().or_model_forward(ids.ctypes.data, B, T, embed, ctypes.cast(arr, ctypes.c_void_p), len(layers),
                            _c(final_norm), _c(lm_head), lm_head.shape[0], d, n_heads, hidden, eps, theta, logits)
     return logits
+
+
+# ---------------------------------------------------------------------------
+# Training path (backward): restatements of FlashAttention.cpp:185-359,
+# OlmoAttention.cpp:149-330 and RMSNorm.cpp:24-41.
+# ---------------------------------------------------------------------------
+
+def sgemm(a, b, trans_a: bool, trans_b: bool, alpha: float = 1.0, c=None, beta: float = 0.0):
+    """Row-major CBLAS sgemm: C = alpha * op(A) op(B) + beta * C."""
+    a, b = _c(a), _c(b)
+    M = a.shape[1] if trans_a else a.shape[0]
+    K = a.shape[0] if trans_a else a.shape[1]
+    N = b.shape[0] if trans_b else b.shape[1]
+    if c is None:
+        c = np.zeros((M, N), np.float32)
+    lib().or_sgemm(int(trans_a), int(trans_b), M, N, K, alpha, a, a.shape[1], b, b.shape[1], beta, c, N)
+    return c
+
+
+def rmsnorm_rms(x, g, eps: float = 1e-6):
+    """RMSNorm forward returning (y, rms per row)."""
+    x = _c(x)
+    rows = x.size // x.shape[-1]
+    y = np.empty_like(x)
+    rms = np.empty(rows, np.float32)
+    lib().or_rmsnorm_rms(x, _c(g), y, rms, rows, x.shape[-1], eps)
+    return y, rms
+
+
+def rmsnorm_bwd(dy, y, g, rms, dg=None):
+    """RMSNorm.cpp:24-36.  Returns (dx, dg) with dg accumulated into the given array."""
+    dy, y = _c(dy), _c(y)
+    dim = y.shape[-1]
+    dx = np.empty_like(dy)
+    if dg is None:
+        dg = np.zeros(dim, np.float32)
+    lib().or_rmsnorm_bwd(dy, y, _c(g), _c(rms), dx, dg, dy.size // dim, dim)
+    return dx, dg
+
+
+def rope_bwd(dy, sin_t=None, cos_t=None):
+    """OlmoAttention.cpp:149-187.  dy: [B,T,H,D]."""
+    dy = _c(dy)
+    B, T, H, D = dy.shape
+    if sin_t is None:
+        sin_t, cos_t = rope_tables(T, D)
+    dx = np.empty_like(dy)
+    lib().or_rope_bwd(dy, dx, B, T, H, D, _c(sin_t), _c(cos_t))
+    return dx
+
+
+def flash_bwd(dout, out, m, l, q, k, v, scale: float, causal: bool = True):
+    """Restated FlashAttention.cpp:185-359.  Returns (dq, dk, dv)."""
+    args = [_c(a) for a in (dout, out, m, l, q, k, v)]
+    B, T, H, D = args[4].shape
+    dq, dk, dv = (np.empty_like(args[4]) for _ in range(3))
+    lib().or_flash_bwd(*args, dq, dk, dv, B, T, H, D, scale, int(causal))
+    return dq, dk, dv
+
+
+def ref_flash_bwd(dout, out, m, l, q, k, v, scale: float, causal: bool = True, threads: int = 0):
+    """The reference's own flash_attention_backward.  Returns (dq, dk, dv, seconds)."""
+    L = ref_lib()
+    if L is None:
+        raise RuntimeError("reference flash library not built (oracle/_ref)")
+    args = [_c(a) for a in (dout, out, m, l, q, k, v)]
+    B, T, H, D = args[4].shape
+    dq, dk, dv = (np.empty_like(args[4]) for _ in range(3))
+    L.ref_set_threads(int(threads))
+    secs = L.ref_flash_backward(*args, dq, dk, dv, B, T, H, D, scale, int(causal))
+    if secs < 0:
+        raise RuntimeError("reference flash_attention_backward raised")
+    return dq, dk, dv, secs
+
+
+def attention_layer_train(x, wq, wk, wv, wo, qg, kg, eps: float = 1e-6, theta: float = 500000.0,
+                          n_heads: int = 16):
+    """OlmoAttention::forward (OlmoAttention.cpp:56-108) keeping the activations
+    its backward reads (OlmoAttention.h:28-38).  Returns (y, saved)."""
+    x = _c(x)
+    B, T, d = x.shape
+    hd = d // n_heads
+    x2 = x.reshape(-1, d)
+    qp, kp, vp = linear(x2, wq), linear(x2, wk), linear(x2, wv)
+    qn, rq = rmsnorm_rms(qp, qg, eps)
+    kn, rk = rmsnorm_rms(kp, kg, eps)
+    s_t, c_t = rope_tables(T, hd, theta)
+    qr = rope(qn.reshape(B, T, n_heads, hd), s_t, c_t)
+    kr = rope(kn.reshape(B, T, n_heads, hd), s_t, c_t)
+    v4 = vp.reshape(B, T, n_heads, hd)
+    scale = 1.0 / np.sqrt(np.float32(hd))
+    o, m, l = flash_fwd(qr, kr, v4, float(scale), True)
+    y = linear(o.reshape(-1, d), wo).reshape(B, T, d)
+    saved = dict(x2=x2, qn=qn, kn=kn, rq=rq, rk=rk, qr=qr, kr=kr, v=v4, o=o, m=m, l=l, sin=s_t, cos=c_t,
+                 scale=float(scale))
+    return y, saved
+
+
+def attention_layer_backward(dy, saved, wq, wk, wv, wo, qg, kg, n_heads: int = 16):
+    """OlmoAttention::backward (OlmoAttention.cpp:189-312).  Returns (dx, grads)
+    with grads = dict(q_proj, k_proj, v_proj, o_proj, q_norm, k_norm)."""
+    dy = _c(dy)
+    B, T, d = dy.shape
+    hd = d // n_heads
+    dy2 = dy.reshape(-1, d)
+    a2 = saved["o"].reshape(-1, d)
+    g = {}
+    g["o_proj"] = sgemm(dy2, a2, True, False)                       # :201-205
+    da = sgemm(dy2, wo, False, False).reshape(B, T, n_heads, hd)  # :207
+    dq_r, dk_r, dv = flash_bwd(da, saved["o"], saved["m"], saved["l"], saved["qr"], saved["kr"], saved["v"],
+                               saved["scale"], True)                # :219-221
+    dq_n = rope_bwd(dq_r, saved["sin"], saved["cos"]).reshape(-1, d)  # :228-229
+    dk_n = rope_bwd(dk_r, saved["sin"], saved["cos"]).reshape(-1, d)
+    dqp, g["q_norm"] = rmsnorm_bwd(dq_n, saved["qn"], qg, saved["rq"])  # :236-237
+    dkp, g["k_norm"] = rmsnorm_bwd(dk_n, saved["kn"], kg, saved["rk"])
+    dv2 = dv.reshape(-1, d)
+    x2 = saved["x2"]
+    g["q_proj"] = sgemm(dqp, x2, True, False)                         # :250-254
+    g["k_proj"] = sgemm(dkp, x2, True, False)
+    g["v_proj"] = sgemm(dv2, x2, True, False)
+    dx = sgemm(dqp, wq, False, False)                                  # :278-298
+    sgemm(dkp, wk, False, False, c=dx, beta=1.0)
+    sgemm(dv2, wv, False, False, c=dx, beta=1.0)
+    return dx.reshape(B, T, d), g

@@ -316,3 +316,170 @@ void or_model_forward(const unsigned* ids, long B, long T, const float* embed, c
     free(y);
     free(t);
 }
+
+/* ------------------------------------------------------------------------
+ * Training path (backward) restatements.
+ * ------------------------------------------------------------------------ */
+
+/* Generic row-major CBLAS sgemm, the form of every projection-gradient call in
+ * OlmoAttention::backward (OlmoAttention.cpp:201-205, 240-267, 278-298). */
+void or_sgemm(int trans_a, int trans_b, int M, int N, int K, float alpha, const float* A, int lda,
+              const float* Bm, int ldb, float beta, float* C, int ldc) {
+    scipy_cblas_sgemm(101, trans_a ? 112 : 111, trans_b ? 112 : 111, M, N, K, alpha, A, lda, Bm, ldb, beta, C,
+                      ldc);
+}
+
+/* RMSNorm forward that also returns the per-row rms (RMSNorm.cpp:15-22, the
+ * m_act_rms member the backward divides by). */
+void or_rmsnorm_rms(const float* x, const float* g, float* y, float* rms_out, long rows, int dim, float eps) {
+#pragma omp parallel for schedule(static)
+    for (long r = 0; r < rows; ++r) {
+        const float* xr = x + (size_t)r * dim;
+        float* yr = y + (size_t)r * dim;
+        float ss = 0.0f;
+        for (int i = 0; i < dim; ++i) ss += xr[i] * xr[i];
+        const float rms = sqrtf(ss / (float)dim + eps);
+        rms_out[r] = rms;
+        for (int i = 0; i < dim; ++i) yr[i] = xr[i] / rms * g[i];
+    }
+}
+
+/* RMSNorm backward, RMSNorm.cpp:24-36, with y = the forward output (x/rms*g):
+ *   c = mean(dy * y) over the row;  x_hat = y / g (recomputed, :30);
+ *   dg += sum over rows of dy * x_hat (:31);  dx = (g*dy - x_hat*c) / rms (:35). */
+void or_rmsnorm_bwd(const float* dy, const float* y, const float* g, const float* rms, float* dx, float* dg,
+                    long rows, int dim) {
+#pragma omp parallel for schedule(static)
+    for (long r = 0; r < rows; ++r) {
+        const float* dyr = dy + (size_t)r * dim;
+        const float* yr = y + (size_t)r * dim;
+        float* dxr = dx + (size_t)r * dim;
+        float c = 0.0f;
+        for (int i = 0; i < dim; ++i) c += dyr[i] * yr[i];
+        c /= (float)dim;
+        for (int i = 0; i < dim; ++i) {
+            const float xh = yr[i] / g[i];
+            dxr[i] = (g[i] * dyr[i] - xh * c) / rms[r];
+        }
+    }
+    /* weight gradient: column sums in row order */
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < dim; ++i) {
+        float acc = 0.0f;
+        for (long r = 0; r < rows; ++r) acc += dy[(size_t)r * dim + i] * (y[(size_t)r * dim + i] / g[i]);
+        dg[i] += acc;
+    }
+}
+
+/* RoPE backward, OlmoAttention.cpp:149-187 (the transpose of the rotation):
+ *   d_in[d]      =  d_out[d]*cos[t][d] + d_out[d+half]*sin[t][d+half]
+ *   d_in[d+half] = -d_out[d]*sin[t][d] + d_out[d+half]*cos[t][d+half]. */
+void or_rope_bwd(const float* dy, float* dx, long B, long T, int H, int D, const float* sin_t,
+                 const float* cos_t) {
+    const int half = D / 2;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (long b = 0; b < B; ++b) {
+        for (long t = 0; t < T; ++t) {
+            for (int h = 0; h < H; ++h) {
+                const size_t base = (((size_t)b * T + t) * H + h) * D;
+                const float* c = cos_t + (size_t)t * D;
+                const float* s = sin_t + (size_t)t * D;
+                for (int d = 0; d < half; ++d) {
+                    dx[base + d] = dy[base + d] * c[d] + dy[base + d + half] * s[d + half];
+                    dx[base + d + half] = -dy[base + d] * s[d] + dy[base + d + half] * c[d + half];
+                }
+            }
+        }
+    }
+}
+
+/* Flash attention backward, FlashAttention.cpp:185-359.  Same blocking
+ * (256 x 256), same skip rule (causal && q_start < k_start, :247), per Q
+ * block: D[i] = O[i].dO[i] (:232-237); per K block: S = scale * Q K^T (:250),
+ * P = exp(s - m)/l or 0 where q_pos < k_pos (:262-275), dP = dO V^T (:278),
+ * dS = P * (dP - D) * scale (:290-296), dV += P^T dO (:299-314),
+ * dQ_block += dS K (:317-325), dK += dS^T Q (:328-343); dQ written per Q
+ * block (:347-351).  Dot products are plain fp32 loops in index order. */
+void or_flash_bwd(const float* dO, const float* O, const float* Mi, const float* Li, const float* Q,
+                  const float* K, const float* V, float* dQ, float* dK, float* dV, long B, long T, int H, int D,
+                  float scale, int causal) {
+    const size_t rs = (size_t)H * D;
+    const size_t nall = (size_t)B * T * H * D;
+    memset(dQ, 0, nall * sizeof(float));
+    memset(dK, 0, nall * sizeof(float));
+    memset(dV, 0, nall * sizeof(float));
+#pragma omp parallel
+    {
+        float* P = (float*)malloc(sizeof(float) * OR_BLK * OR_BLK);
+        float* dS = (float*)malloc(sizeof(float) * OR_BLK * OR_BLK);
+        float* Dr = (float*)malloc(sizeof(float) * OR_BLK);
+        float* dQb = (float*)malloc(sizeof(float) * OR_BLK * D);
+#pragma omp for schedule(dynamic, 1)
+        for (long bh = 0; bh < B * H; ++bh) {
+            const long b = bh / H;
+            const int h = (int)(bh % H);
+            for (long q0 = 0; q0 < T; q0 += OR_BLK) {
+                const long Br = (T - q0) < OR_BLK ? (T - q0) : OR_BLK;
+                for (long i = 0; i < Br; ++i) {
+                    const size_t ro = ((size_t)b * T + q0 + i) * rs + (size_t)h * D;
+                    float acc = 0.0f;
+                    for (int d = 0; d < D; ++d) acc += O[ro + d] * dO[ro + d];
+                    Dr[i] = acc;
+                }
+                memset(dQb, 0, sizeof(float) * Br * D);
+                for (long k0 = 0; k0 < T; k0 += OR_BLK) {
+                    const long Bc = (T - k0) < OR_BLK ? (T - k0) : OR_BLK;
+                    if (causal && q0 < k0) continue;
+                    for (long i = 0; i < Br; ++i) {
+                        const size_t rq = ((size_t)b * T + q0 + i) * rs + (size_t)h * D;
+                        const size_t ist = ((size_t)b * T + q0 + i) * H + h;
+                        const float m = Mi[ist], l = Li[ist], Di = Dr[i];
+                        for (long j = 0; j < Bc; ++j) {
+                            const size_t rk = ((size_t)b * T + k0 + j) * rs + (size_t)h * D;
+                            float p = 0.0f, dp = 0.0f;
+                            if (!(causal && q0 + i < k0 + j)) {
+                                float s = 0.0f;
+                                for (int d = 0; d < D; ++d) s += Q[rq + d] * K[rk + d];
+                                p = expf(scale * s - m) / l;
+                            }
+                            for (int d = 0; d < D; ++d) dp += dO[rq + d] * V[rk + d];
+                            P[i * OR_BLK + j] = p;
+                            dS[i * OR_BLK + j] = p * (dp - Di) * scale;
+                        }
+                    }
+                    for (long j = 0; j < Bc; ++j) {
+                        const size_t rk = ((size_t)b * T + k0 + j) * rs + (size_t)h * D;
+                        for (int d = 0; d < D; ++d) {
+                            float av = 0.0f, ak = 0.0f;
+                            for (long i = 0; i < Br; ++i) {
+                                const size_t rq = ((size_t)b * T + q0 + i) * rs + (size_t)h * D;
+                                av += P[i * OR_BLK + j] * dO[rq + d];
+                                ak += dS[i * OR_BLK + j] * Q[rq + d];
+                            }
+                            dV[rk + d] += av;
+                            dK[rk + d] += ak;
+                        }
+                    }
+                    for (long i = 0; i < Br; ++i) {
+                        for (int d = 0; d < D; ++d) {
+                            float acc = 0.0f;
+                            for (long j = 0; j < Bc; ++j) {
+                                const size_t rk = ((size_t)b * T + k0 + j) * rs + (size_t)h * D;
+                                acc += dS[i * OR_BLK + j] * K[rk + d];
+                            }
+                            dQb[i * D + d] += acc;
+                        }
+                    }
+                }
+                for (long i = 0; i < Br; ++i) {
+                    const size_t rq = ((size_t)b * T + q0 + i) * rs + (size_t)h * D;
+                    for (int d = 0; d < D; ++d) dQ[rq + d] = dQb[i * D + d];
+                }
+            }
+        }
+        free(P);
+        free(dS);
+        free(Dr);
+        free(dQb);
+    }
+}
