@@ -5,12 +5,14 @@ as hand-written tcgen05/TMA kernels behind the C ABI in include/dirktensor_b200.
 """
 from ._lib import DTError, lib  # noqa: F401  (loads the CUDA library; raises if unbuilt)
 from .attention import (  # noqa: F401
+    FlashAttentionGradients,
     FlashAttentionResult,
     OlmoAttention,
     OlmoModel,
     cast_bf16,
     check_device_error,
     d_model,
+    flash_attention_backward,
     flash_attention_forward,
     flash_attention_forward_bf16,
     gemm_bf16_tn,

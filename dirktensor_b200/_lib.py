@@ -87,6 +87,9 @@ SIGNATURES = {
     "dt_flash_fwd_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "dt_flash_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P, _SZ, _P]),
     "dt_flash_fwd_host": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I]),
+    "dt_flash_bwd_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "dt_flash_bwd": (_I, [_P] * 10 + [_I, _I, _I, _I, _F, _I, _P, _SZ, _P]),
+    "dt_flash_bwd_host": (_I, [_P] * 10 + [_I, _I, _I, _I, _F, _I]),
     "dt_flash_fwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "dt_flash_fwd_bf16_exchange": (_I, [_P, _P, _P, ctypes.POINTER(_P), _I, _I, _LL, _P, _P, _I, _I, _I, _I, _F, _I,
                                         _P]),

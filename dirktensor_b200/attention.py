@@ -111,6 +111,52 @@ def flash_attention_forward(Q, K, V, scale: float, causal: bool = True) -> Flash
     return FlashAttentionResult(out, m, l)
 
 
+class FlashAttentionGradients(NamedTuple):
+    """Mirror of FlashAttentionGradients (FlashAttention.h:27-31)."""
+    d_Q: object
+    d_K: object
+    d_V: object
+
+
+def flash_attention_backward(d_output, output, softmax_m, softmax_l, Q, K, V, scale: float,
+                             causal: bool = True) -> FlashAttentionGradients:
+    """Drop-in for flash_attention_backward (FlashAttention.h:33-43).
+
+    All tensors float32: d_output, output, Q, K, V [B, T, H, D] (D = 128);
+    softmax_m, softmax_l [B, T, H] as flash_attention_forward returns them.
+    Operands are rounded to bf16 for the tensor cores; the softmax recomputation
+    and D = rowsum(output * d_output) are fp32.
+    """
+    names = ("d_output", "output", "Q", "K", "V")
+    if _is_torch(Q):
+        torch = _torch()
+        for n, t in zip(names, (d_output, output, Q, K, V)):
+            _need_cuda_f32(n, t, 4)
+        _need_cuda_f32("softmax_m", softmax_m, 3)
+        _need_cuda_f32("softmax_l", softmax_l, 3)
+        B, T, H, D = Q.shape
+        for t in (d_output, output, K, V):
+            if t.shape != Q.shape:
+                raise ValueError("d_output, output, Q, K, V shapes differ")
+        dq, dk, dv = (torch.empty_like(Q) for _ in range(3))
+        nbytes = lib().dt_flash_bwd_workspace_bytes(B, T, H, D)
+        ws = _workspace(Q.device, nbytes)
+        check(lib().dt_flash_bwd(d_output.data_ptr(), output.data_ptr(), softmax_m.data_ptr(),
+                                 softmax_l.data_ptr(), Q.data_ptr(), K.data_ptr(), V.data_ptr(), dq.data_ptr(),
+                                 dk.data_ptr(), dv.data_ptr(), B, T, H, D, float(scale), int(bool(causal)),
+                                 ws.data_ptr(), ws.numel(), _stream_ptr(Q.device)))
+        return FlashAttentionGradients(dq, dk, dv)
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (d_output, output, softmax_m, softmax_l, Q, K, V)]
+    B, T, H, D = arrs[4].shape
+    for a in (arrs[0], arrs[1], arrs[5], arrs[6]):
+        if a.shape != arrs[4].shape:
+            raise ValueError("d_output, output, Q, K, V shapes differ")
+    dq, dk, dv = (np.empty_like(arrs[4]) for _ in range(3))
+    check(lib().dt_flash_bwd_host(*[a.ctypes.data for a in arrs], dq.ctypes.data, dk.ctypes.data, dv.ctypes.data,
+                                  B, T, H, D, float(scale), int(bool(causal))))
+    return FlashAttentionGradients(dq, dk, dv)
+
+
 def flash_attention_forward_bf16(q, k, v, scale: float, causal: bool = True, out=None, out_bf16: bool = False,
                                  out_row_stride: Optional[int] = None, softmax_m=None, softmax_l=None,
                                  seq_lens=None):

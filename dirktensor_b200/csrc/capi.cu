@@ -15,6 +15,7 @@
 
 #include "../../include/dirktensor_b200.h"
 #include "dt_common.cuh"
+#include "flash_bwd.cuh"
 #include "flash_fwd.cuh"
 #include "gemm.cuh"
 #include "gemm2sm.cuh"
@@ -153,6 +154,8 @@ std::mutex g_mu;
 DevState g_dev[64];
 
 constexpr size_t kFlashSmem = sizeof(dt::flash::Smem) + 1024;
+constexpr size_t kFlashBwdKvSmem = sizeof(dt::flash_bwd::SmemKV) + 1024;
+constexpr size_t kFlashBwdQSmem = sizeof(dt::flash_bwd::SmemQ) + 1024;
 constexpr size_t kGemmSmem = sizeof(dt::gemm::SmemT<dt::gemm::kBN>) + 1024;
 constexpr size_t kGemmNarrowSmem = sizeof(dt::gemm::SmemT<dt::gemm::kNarrowBN>) + 1024;
 constexpr size_t kGemm2Smem = sizeof(dt::gemm2::Smem) + 1024;
@@ -179,6 +182,10 @@ int ensure_attrs(int dev) {
         return fail(DT_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
                     prop.major, prop.minor);
     s.num_sms = prop.multiProcessorCount;
+    DT_CUDA(cudaFuncSetAttribute(dt::flash_bwd::flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kFlashBwdKvSmem));
+    DT_CUDA(cudaFuncSetAttribute(dt::flash_bwd::flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kFlashBwdQSmem));
     DT_CUDA(cudaFuncSetAttribute(dt::flash::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kFlashSmem));
     DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kBN>,
@@ -344,6 +351,67 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     const long long grid = (long long)p.nblk * B * H;
     if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
     dt::flash::flash_fwd_kernel<<<(unsigned)grid, dt::flash::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+// Attention backward on bf16 Q/K/V.  dout fp32 [B,T,H,D]; O fp32 (out) or bf16
+// (out_bf16) with row stride out_row_stride; m, l [B,T,H]; dq/dk/dv fp32
+// [B,T,H,D].  Scratch: dob (bf16 [B,T,H,D]), dvec and lse2 ([B,H,Tpad] fp32).
+size_t flash_bwd_rows_bytes(int B, int T, int H) {
+    const long long Tpad = (long long)((T + 127) / 128) * 128;
+    return align256((size_t)B * H * Tpad * 4);
+}
+
+int launch_flash_bwd(const void* qb, const void* kb, const void* vb, const float* dout, const float* out,
+                     const void* out_bf16, long long out_row_stride, const float* m, const float* l, float* dq,
+                     float* dk, float* dv, int B, int T, int H, float scale, int causal, void* dob, float* dvec,
+                     float* lse2, cudaStream_t st) {
+    if ((long long)B * T * H == 0) return DT_OK;
+    const int nblk = (T + 127) / 128;
+    dt::flash_bwd::PreParams pp{};
+    pp.out = out;
+    pp.out_bf16 = reinterpret_cast<const __nv_bfloat16*>(out_bf16);
+    pp.out_row_stride = out_row_stride;
+    pp.dout = dout;
+    pp.m = m;
+    pp.l = l;
+    pp.dout_bf16 = reinterpret_cast<__nv_bfloat16*>(dob);
+    pp.dvec = dvec;
+    pp.lse2 = lse2;
+    pp.B = B;
+    pp.T = T;
+    pp.H = H;
+    pp.Tpad = nblk * 128;
+    const long long rows = (long long)B * H * pp.Tpad;
+    dt::flash_bwd::flash_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(pp);
+    DT_CUDA(cudaGetLastError());
+    CUtensorMap mq, mk, mv, mdo;
+    DT_TRY(make_map_bthd(&mq, qb, B, T, H, 128));
+    DT_TRY(make_map_bthd(&mk, kb, B, T, H, 128));
+    DT_TRY(make_map_bthd(&mv, vb, B, T, H, 128));
+    DT_TRY(make_map_bthd(&mdo, dob, B, T, H, 128));
+    dt::flash_bwd::Params p{};
+    p.B = B;
+    p.T = T;
+    p.H = H;
+    p.nblk = nblk;
+    p.Tpad = pp.Tpad;
+    p.causal = causal ? 1 : 0;
+    p.scale = scale;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.dvec = dvec;
+    p.lse2 = lse2;
+    p.dq = dq;
+    p.dk = dk;
+    p.dv = dv;
+    const long long grid = (long long)nblk * B * H;
+    if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
+    dt::flash_bwd::flash_bwd_dkdv_kernel<<<(unsigned)grid, dt::flash_bwd::kThreads, kFlashBwdKvSmem, st>>>(
+        mq, mk, mv, mdo, p);
+    DT_CUDA(cudaGetLastError());
+    dt::flash_bwd::flash_bwd_dq_kernel<<<(unsigned)grid, dt::flash_bwd::kThreads, kFlashBwdQSmem, st>>>(mq, mk, mv,
+                                                                                                      mdo, p);
     DT_CUDA(cudaGetLastError());
     return DT_OK;
 }
@@ -571,6 +639,80 @@ int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, 
     DT_CUDA(cudaMemcpyAsync(o, dout, n * 4, cudaMemcpyDeviceToHost, st));
     if (softmax_m) DT_CUDA(cudaMemcpyAsync(softmax_m, dm, ns * 4, cudaMemcpyDeviceToHost, st));
     if (softmax_l) DT_CUDA(cudaMemcpyAsync(softmax_l, dl, ns * 4, cudaMemcpyDeviceToHost, st));
+    DT_CUDA(cudaStreamSynchronize(st));
+    bool had;
+    return read_device_error(&had);
+}
+
+// ---- flash attention backward ---------------------------------------------
+
+size_t dt_flash_bwd_workspace_bytes(int B, int T, int H, int D) {
+    if (B <= 0 || T <= 0 || H <= 0 || D <= 0) return 0;
+    return 4 * align256((size_t)B * T * H * D * 2) + 2 * flash_bwd_rows_bytes(B, T, H);
+}
+
+int dt_flash_bwd(const float* dout, const float* out, const float* softmax_m, const float* softmax_l,
+                 const float* q, const float* k, const float* v, float* dq, float* dk, float* dv, int B, int T,
+                 int H, int D, float scale, int causal, void* workspace, size_t workspace_bytes, void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    const void* ptrs[] = {dout, out, softmax_m, softmax_l, q, k, v, dq, dk, dv};
+    for (const void* ptr : ptrs)
+        if (!ptr || !aligned16(ptr)) return fail(DT_ERR_INVALID_ARGUMENT, "null or unaligned (16 B) argument");
+    const size_t need = dt_flash_bwd_workspace_bytes(B, T, H, D);
+    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+        return fail(DT_ERR_INVALID_ARGUMENT, "workspace must be >= %zu bytes and 16-byte aligned", need);
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const long long n = (long long)B * T * H * D;
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    const size_t one = align256((size_t)n * 2), rows = flash_bwd_rows_bytes(B, T, H);
+    DT_TRY(launch_cast3(q, k, v, ws, ws + one, ws + 2 * one, n, st));
+    return launch_flash_bwd(ws, ws + one, ws + 2 * one, dout, out, nullptr, (long long)H * D, softmax_m, softmax_l,
+                            dq, dk, dv, B, T, H, scale, causal, ws + 3 * one,
+                            reinterpret_cast<float*>(ws + 4 * one), reinterpret_cast<float*>(ws + 4 * one + rows),
+                            st);
+}
+
+int dt_flash_bwd_host(const float* dout, const float* out, const float* softmax_m, const float* softmax_l,
+                      const float* q, const float* k, const float* v, float* dq, float* dk, float* dv, int B, int T,
+                      int H, int D, float scale, int causal) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    const void* ptrs[] = {dout, out, softmax_m, softmax_l, q, k, v, dq, dk, dv};
+    for (const void* ptr : ptrs)
+        if (!ptr) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    const size_t n = (size_t)B * T * H * D, ns = (size_t)B * T * H;
+    const size_t t_bytes = align256(n * 4), s_bytes = align256(ns * 4);
+    const size_t ws = dt_flash_bwd_workspace_bytes(B, T, H, D);
+    std::lock_guard<std::mutex> lk(g_mu);
+    void* stage;
+    cudaStream_t st;
+    // device copies: dout, out, q, k, v (in), dq, dk, dv (out), m, l, then the workspace
+    DT_TRY(ensure_stage(dev, 8 * t_bytes + 2 * s_bytes + ws, &stage, &st));
+    uint8_t* base = reinterpret_cast<uint8_t*>(stage);
+    float* d[8];
+    for (int i = 0; i < 8; ++i) d[i] = reinterpret_cast<float*>(base + i * t_bytes);
+    float* dm = reinterpret_cast<float*>(base + 8 * t_bytes);
+    float* dl = reinterpret_cast<float*>(base + 8 * t_bytes + s_bytes);
+    uint8_t* w = base + 8 * t_bytes + 2 * s_bytes;
+    const float* hin[5] = {dout, out, q, k, v};
+    for (int i = 0; i < 5; ++i) DT_CUDA(cudaMemcpyAsync(d[i], hin[i], n * 4, cudaMemcpyHostToDevice, st));
+    DT_CUDA(cudaMemcpyAsync(dm, softmax_m, ns * 4, cudaMemcpyHostToDevice, st));
+    DT_CUDA(cudaMemcpyAsync(dl, softmax_l, ns * 4, cudaMemcpyHostToDevice, st));
+    const size_t one = align256(n * 2), rows = flash_bwd_rows_bytes(B, T, H);
+    DT_TRY(launch_cast3(d[2], d[3], d[4], w, w + one, w + 2 * one, (long long)n, st));
+    DT_TRY(launch_flash_bwd(w, w + one, w + 2 * one, d[0], d[1], nullptr, (long long)H * D, dm, dl, d[5], d[6], d[7],
+                            B, T, H, scale, causal, w + 3 * one, reinterpret_cast<float*>(w + 4 * one),
+                            reinterpret_cast<float*>(w + 4 * one + rows), st));
+    DT_CUDA(cudaMemcpyAsync(dq, d[5], n * 4, cudaMemcpyDeviceToHost, st));
+    DT_CUDA(cudaMemcpyAsync(dk, d[6], n * 4, cudaMemcpyDeviceToHost, st));
+    DT_CUDA(cudaMemcpyAsync(dv, d[7], n * 4, cudaMemcpyDeviceToHost, st));
     DT_CUDA(cudaStreamSynchronize(st));
     bool had;
     return read_device_error(&had);

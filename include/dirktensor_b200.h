@@ -72,6 +72,22 @@ int dt_flash_fwd(const float* q, const float* k, const float* v, float* o, float
 int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, float* softmax_m,
                       float* softmax_l, int B, int T, int H, int D, float scale, int causal);
 
+/* Replaces flash_attention_backward (FlashAttention.h:33-43,
+ * FlashAttention.cpp:185-359): from the upstream gradient dout, the forward
+ * output out and statistics softmax_m / softmax_l (as dt_flash_fwd writes
+ * them), and q, k, v, computes dq, dk, dv ([B,T,H,D] fp32 device arrays).
+ * Operands are rounded to bf16 for the tensor cores; D = rowsum(out*dout) and
+ * the softmax recomputation are fp32.  workspace: >= dt_flash_bwd_workspace_bytes,
+ * 16-byte aligned.  Asynchronous on `stream`. */
+size_t dt_flash_bwd_workspace_bytes(int B, int T, int H, int D);
+int dt_flash_bwd(const float* dout, const float* out, const float* softmax_m, const float* softmax_l,
+                 const float* q, const float* k, const float* v, float* dq, float* dk, float* dv, int B, int T,
+                 int H, int D, float scale, int causal, void* workspace, size_t workspace_bytes, void* stream);
+/* Same with host buffers (the call the C++ drop-in flash_attention_backward makes). */
+int dt_flash_bwd_host(const float* dout, const float* out, const float* softmax_m, const float* softmax_l,
+                      const float* q, const float* k, const float* v, float* dq, float* dk, float* dv, int B, int T,
+                      int H, int D, float scale, int causal);
+
 /* Same as dt_flash_fwd, but allocates nothing and takes no workspace: the
  * bf16 operand copies live in a fixed 24 MiB array inside the library's device
  * image (present on every GPU that loads the library until exit).  No

@@ -14,6 +14,7 @@ TOL_M_ABS = 5e-2          # softmax_m (scaled-score units)
 TOL_L_REL = 2e-2          # softmax_l, relative
 TOL_LAYER_REL_L2 = 1.5e-2  # attention layer output y, relative L2
 TOL_GEMM_REL_L2 = 1e-5    # GEMM vs fp32 matmul of the same bf16-rounded operands
+TOL_BWD_REL_L2 = 2e-2    # attention gradients dQ, dK, dV, relative L2 (bf16 Q/K/V/dO/P/dS operands)
 
 
 def randn(seed: int, shape, scale: float = 1.0) -> np.ndarray:
