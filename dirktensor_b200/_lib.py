@@ -87,6 +87,7 @@ SIGNATURES = {
     "dt_flash_fwd_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "dt_flash_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P, _SZ, _P]),
     "dt_flash_fwd_host": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I]),
+    "dt_gemm_bf16": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _LL, _P]),
     "dt_flash_bwd_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "dt_flash_bwd": (_I, [_P] * 10 + [_I, _I, _I, _I, _F, _I, _P, _SZ, _P]),
     "dt_flash_bwd_host": (_I, [_P] * 10 + [_I, _I, _I, _I, _F, _I]),
@@ -101,6 +102,11 @@ SIGNATURES = {
     "dt_attn_create_from_npy": (_I, [ctypes.c_char_p, ctypes.c_uint, _I, ctypes.POINTER(_P)]),
     "dt_attn_forward": (_I, [_P, _P, _I, _I, _P, _P, _P]),
     "dt_attn_forward_host": (_I, [_P, _P, _I, _I, _P, _P]),
+    "dt_attn_backward": (_I, [_P, _P, _I, _I, _P, _P]),
+    "dt_attn_backward_host": (_I, [_P, _P, _I, _I, _P]),
+    "dt_attn_step": (_I, [_P, _F, _P]),
+    "dt_attn_zero_grad": (_I, [_P, _P]),
+    "dt_attn_get_params_host": (_I, [_P] * 7 + [_I]),
     "dt_attn_destroy": (_I, [_P]),
     "dt_model_create": (_I, [ctypes.POINTER(dt_model_weights), _I, ctypes.POINTER(_P)]),
     "dt_model_create_from_npy": (_I, [ctypes.c_char_p, _I, _I, ctypes.POINTER(_P)]),

@@ -198,6 +198,26 @@ def gemm_bf16_tn(A, B, out_bf16: bool = False, out=None):
     return out
 
 
+def gemm_bf16(A, B, a_mn: bool = False, b_mn: bool = False, out=None, accumulate: bool = False,
+              out_bf16: bool = False):
+    """C (+)= op(A) . op(B)^T with bf16 CUDA operands.  A is [M, K] (a_mn False)
+    or stored [K, M] (a_mn True); B is [N, K] (b_mn False) or stored [K, N]
+    (b_mn True).  accumulate adds into the given fp32 `out`."""
+    torch = _torch()
+    M, K = (A.shape[1], A.shape[0]) if a_mn else (A.shape[0], A.shape[1])
+    N = B.shape[1] if b_mn else B.shape[0]
+    if (B.shape[0] if b_mn else B.shape[1]) != K:
+        raise ValueError("inner dimensions differ")
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate needs an out tensor")
+        out = torch.empty((M, N), dtype=torch.bfloat16 if out_bf16 else torch.float32, device=A.device)
+    mode = 2 if accumulate else (1 if out_bf16 else 0)
+    check(lib().dt_gemm_bf16(A.data_ptr(), int(a_mn), B.data_ptr(), int(b_mn), out.data_ptr(), mode, M, N, K,
+                             out.stride(0), _stream_ptr(A.device)))
+    return out
+
+
 def qk_norm_rope(q, k, v, q_gain, k_gain, B: int, T: int, eps: float = rms_eps, theta: float = rope_theta):
     """Prologue on fp32 rows (row stride taken from q): returns bf16 (q, k, v) [B*T, 2048]."""
     torch = _torch()
@@ -223,7 +243,7 @@ def check_device_error() -> None:
 
 
 class OlmoAttention:
-    """Drop-in for OlmoAttention (OlmoAttention.h:10-42), forward/prefill path.
+    """Drop-in for OlmoAttention (OlmoAttention.h:10-42): forward, backward, step, zero_grad.
 
     ``OlmoAttention(folder, index)`` loads the six ``.npy`` weight files of
     layer ``index`` as OlmoAttention.cpp:39-46 does; ``OlmoAttention.from_weights``
@@ -283,15 +303,42 @@ class OlmoAttention:
 
     __call__ = forward
 
-    def backward(self, d_output):
-        """The training path (OlmoAttention.cpp:149-312) is not part of this build."""
-        raise NotImplementedError("OlmoAttention.backward: only the forward (prefill) path is implemented")
+    def backward(self, d_output, out=None):
+        """OlmoAttention::backward (OlmoAttention.cpp:189-312): gradient of the
+        last forward's input, given d_output [B, T, 2048] float32 of that
+        forward's shape (a forward without seq_lens).  Weight gradients
+        accumulate in the handle until zero_grad()."""
+        if _is_torch(d_output):
+            torch = _torch()
+            _need_cuda_f32("d_output", d_output, 3)
+            B, T, _ = d_output.shape
+            dx = out if out is not None else torch.empty_like(d_output)
+            check(lib().dt_attn_backward(self._h, d_output.data_ptr(), B, T, dx.data_ptr(),
+                                         _stream_ptr(d_output.device)))
+            return dx
+        dy = np.ascontiguousarray(d_output, dtype=np.float32)
+        B, T, _ = dy.shape
+        dx = np.empty_like(dy)
+        check(lib().dt_attn_backward_host(self._h, dy.ctypes.data, B, T, dx.ctypes.data))
+        return dx
 
-    def step(self, lr: float):
-        raise NotImplementedError("OlmoAttention.step: only the forward (prefill) path is implemented")
+    def step(self, lr: float, stream=None):
+        """SGD step w -= lr * grad on every parameter (OlmoAttention.cpp:315-322)."""
+        check(lib().dt_attn_step(self._h, float(lr), stream))
 
-    def zero_grad(self):
-        """No gradients are kept on the forward-only path; nothing to clear."""
+    def zero_grad(self, stream=None):
+        """Clears the accumulated gradients (OlmoAttention.cpp:324-330)."""
+        check(lib().dt_attn_zero_grad(self._h, stream))
+
+    def parameters(self, gradients: bool = False) -> dict:
+        """Host copies of the fp32 weights (or of their gradients) keyed like the checkpoint."""
+        d = d_model
+        out = {k: np.empty((d, d), np.float32) for k in ("q_proj", "k_proj", "v_proj", "o_proj")}
+        out.update({k: np.empty(d, np.float32) for k in ("q_norm", "k_norm")})
+        check(lib().dt_attn_get_params_host(self._h, *(out[k].ctypes.data for k in
+                                                      ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm")),
+                                            int(gradients)))
+        return out
 
     def close(self):
         if self._h:

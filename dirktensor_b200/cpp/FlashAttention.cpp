@@ -23,9 +23,23 @@ FlashAttentionResult flash_attention_forward(const xt::xtensor<float, 4>& Q, con
     return r;
 }
 
-FlashAttentionGradients flash_attention_backward(const xt::xtensor<float, 4>&, const xt::xtensor<float, 4>&,
-                                                 const xt::xtensor<float, 3>&, const xt::xtensor<float, 3>&,
-                                                 const xt::xtensor<float, 4>&, const xt::xtensor<float, 4>&,
-                                                 const xt::xtensor<float, 4>&, float, bool) {
-    throw std::logic_error("flash_attention_backward: the B200 drop-in implements the forward path only");
+FlashAttentionGradients flash_attention_backward(const xt::xtensor<float, 4>& d_output,
+                                                 const xt::xtensor<float, 4>& output,
+                                                 const xt::xtensor<float, 3>& softmax_m,
+                                                 const xt::xtensor<float, 3>& softmax_l,
+                                                 const xt::xtensor<float, 4>& Q, const xt::xtensor<float, 4>& K,
+                                                 const xt::xtensor<float, 4>& V, float scale, bool causal) {
+    const std::size_t b = Q.shape(0), t = Q.shape(1), h = Q.shape(2), d = Q.shape(3);
+    for (const auto* x : {&d_output, &output, &K, &V})
+        if (x->shape() != Q.shape())
+            throw std::invalid_argument("flash_attention_backward: d_output, output, Q, K, V shapes differ");
+    FlashAttentionGradients g;
+    g.d_Q = xt::empty<float>({b, t, h, d});
+    g.d_K = xt::empty<float>({b, t, h, d});
+    g.d_V = xt::empty<float>({b, t, h, d});
+    if (dt_flash_bwd_host(d_output.data(), output.data(), softmax_m.data(), softmax_l.data(), Q.data(), K.data(),
+                          V.data(), g.d_Q.data(), g.d_K.data(), g.d_V.data(), static_cast<int>(b),
+                          static_cast<int>(t), static_cast<int>(h), static_cast<int>(d), scale, causal ? 1 : 0) != DT_OK)
+        throw std::runtime_error(std::string("flash_attention_backward: ") + dt_last_error());
+    return g;
 }

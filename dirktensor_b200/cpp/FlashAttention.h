@@ -26,8 +26,9 @@ struct FlashAttentionGradients {
     xt::xtensor<float, 4> d_V;
 };
 
-// Declared for source compatibility (FlashAttention.h:33-43).  The B200 build
-// covers the forward (prefill) path only; calling this throws std::logic_error.
+// Attention backward (FlashAttention.h:33-43): dQ, dK, dV from the upstream
+// gradient, the forward output and its statistics.  Throws std::runtime_error
+// with the library's message on failure.
 FlashAttentionGradients flash_attention_backward(const xt::xtensor<float, 4>& d_output,
                                                  const xt::xtensor<float, 4>& output,
                                                  const xt::xtensor<float, 3>& softmax_m,

@@ -1,4 +1,5 @@
-// OlmoAttention over the C ABI (dt_attn_create_from_npy / dt_attn_forward_host).
+// OlmoAttention over the C ABI (dt_attn_create_from_npy, dt_attn_forward_host,
+// dt_attn_backward_host, dt_attn_step, dt_attn_zero_grad).
 #include "OlmoAttention.h"
 
 #include <cstdlib>
@@ -46,12 +47,20 @@ xt::xtensor<float, 3> OlmoAttention::forward(const xt::xtensor<float, 3>& input)
     return out;
 }
 
-xt::xtensor<float, 3> OlmoAttention::backward(const xt::xtensor<float, 3>&) {
-    throw std::logic_error("OlmoAttention::backward: the B200 drop-in implements the forward path only");
+xt::xtensor<float, 3> OlmoAttention::backward(const xt::xtensor<float, 3>& d_output) {
+    const std::size_t b = d_output.shape(0), t = d_output.shape(1), d = d_output.shape(2);
+    if (d != d_model) throw std::invalid_argument("OlmoAttention::backward: last dimension must be d_model");
+    xt::xtensor<float, 3> d_input = xt::empty<float>({b, t, d});
+    if (dt_attn_backward_host(m_handle, d_output.data(), static_cast<int>(b), static_cast<int>(t),
+                              d_input.data()) != DT_OK)
+        raise("OlmoAttention::backward");
+    return d_input;
 }
 
-void OlmoAttention::step(float) {
-    throw std::logic_error("OlmoAttention::step: the B200 drop-in implements the forward path only");
+void OlmoAttention::step(float lr) {
+    if (dt_attn_step(m_handle, lr, nullptr) != DT_OK) raise("OlmoAttention::step");
 }
 
-void OlmoAttention::zero_grad() {}
+void OlmoAttention::zero_grad() {
+    if (dt_attn_zero_grad(m_handle, nullptr) != DT_OK) raise("OlmoAttention::zero_grad");
+}

@@ -2,7 +2,8 @@
 // public interface, so OlmoBlock (which holds it by value, OlmoBlock.h:19, and
 // calls forward/backward/step/zero_grad, OlmoBlock.cpp:6-40) compiles
 // unchanged.  The weights live on the GPU (bf16 projections, fp32 norm gains)
-// behind an opaque handle of the C ABI; the class is therefore move-only.
+// behind an opaque handle of the C ABI (with the fp32 master weights and
+// gradients of the training path); the class is therefore move-only.
 #pragma once
 
 #include <string>
@@ -24,10 +25,12 @@ public:
 
     // input (batch, seq, d_model) -> (batch, seq, d_model)  (OlmoAttention.cpp:56-108)
     xt::xtensor<float, 3> forward(const xt::xtensor<float, 3>& input);
-    // Training path (OlmoAttention.cpp:149-330): not provided; throws std::logic_error.
+    // Gradient of the last forward's input (OlmoAttention.cpp:189-312); the
+    // weight gradients accumulate on the GPU until zero_grad().
     xt::xtensor<float, 3> backward(const xt::xtensor<float, 3>& d_output);
+    // w -= lr * grad for every parameter (OlmoAttention.cpp:315-322).
     void step(float lr);
-    // No gradients are held on the forward-only path: nothing to clear.
+    // Clears the accumulated gradients (OlmoAttention.cpp:324-330).
     void zero_grad();
 
 private:

@@ -420,7 +420,7 @@ int launch_flash_bwd(const void* qb, const void* kb, const void* vb, const float
 // sequence's padding are skipped (and written as zeros when pad_zero).
 int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N, int K, long long ldc,
                 cudaStream_t st, int a_planes = 1, int epilogue = dt::gemm::kStore, const int* seq_lens = nullptr,
-                int seq_T = 0, int pad_zero = 0) {
+                int seq_T = 0, int pad_zero = 0, int a_mn = 0, int b_mn = 0) {
     if (M == 0 || N == 0) return DT_OK;
     CUtensorMap ma, mb;
     const int plane_k = K / a_planes;
@@ -432,13 +432,17 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     // the wide tiles would leave SMs idle (the SwiGLU epilogue needs 256 columns).
     const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
     const long long wide_tiles = (long long)((M + 127) / 128) * ((N + 255) / 256);
-    const bool pair = M >= DT_GEMM_2SM_MIN_M && pair_tiles >= nsm / 2;
-    const bool narrow = !pair && epilogue == dt::gemm::kStore && wide_tiles < nsm;
+    // (MN-major operands run on the one-SM kernel)
+    const bool pair = M >= DT_GEMM_2SM_MIN_M && pair_tiles >= nsm / 2 && !a_mn && !b_mn;
+    const bool narrow = !pair && epilogue != dt::gemm::kSwiGLU && wide_tiles < nsm;
     const int bn = narrow ? dt::gemm::kNarrowBN : dt::gemm::kBN;
     // boxes: 128 rows of A and bn rows of B per CTA, or 128 and 128 on SM pairs
-    if (a_planes > 1) DT_TRY(make_map_planar(&ma, A, M, plane_k, a_planes));
+    // MN-major operands ([K, M] / [K, N] row-major): 64 x 64 boxes
+    if (a_mn) DT_TRY(make_map_2d(&ma, A, K, M, 64));
+    else if (a_planes > 1) DT_TRY(make_map_planar(&ma, A, M, plane_k, a_planes));
     else DT_TRY(make_map_2d(&ma, A, M, K, dt::gemm::kBM));
-    DT_TRY(make_map_2d(&mb, Bm, N, K, pair ? dt::gemm2::kHalf : bn));
+    if (b_mn) DT_TRY(make_map_2d(&mb, Bm, K, N, 64));
+    else DT_TRY(make_map_2d(&mb, Bm, N, K, pair ? dt::gemm2::kHalf : bn));
     dt::gemm::Params p{};
     p.M = M;
     p.N = N;
@@ -448,6 +452,8 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     p.c_bf16 = c_bf16;
     p.a_plane_k = a_planes > 1 ? plane_k : 0;
     p.epilogue = epilogue;
+    p.a_mn = a_mn;
+    p.b_mn = b_mn;
     // tiles are 256 rows on SM pairs, 128 on one SM: skip only if they never straddle sequences
     const int tile_rows = pair ? dt::gemm2::kBM : dt::gemm::kBM;
     if (seq_lens && seq_T > 0 && (seq_T % tile_rows) == 0) {
@@ -543,6 +549,13 @@ struct dt_attn {
     void* io = nullptr;  // host-API staging: x, y, seq_lens
     size_t io_bytes = 0;
     cudaStream_t stream = nullptr;
+    // training path (OlmoAttention::backward / step / zero_grad)
+    float* master = nullptr;  // fp32 weights [Wq; Wk; Wv] [3d, d] then Wo [d, d] (the bf16 copies derive from these)
+    float* grad = nullptr;    // fp32 gradients: [3d, d] | [d, d] | q_norm [d] | k_norm [d]
+    void* bws = nullptr;      // backward scratch
+    size_t bws_bytes = 0;
+    int last_B = 0, last_T = 0;  // shape of the last forward, whose activations the workspace holds
+    bool last_varlen = false;
 };
 
 extern "C" {
@@ -899,6 +912,25 @@ int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, in
     return launch_gemm(A, B, C, c_bf16 ? 1 : 0, M, N, K, ldc, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int dt_gemm_bf16(const void* A, int a_mn, const void* B, int b_mn, void* C, int c_mode, int M, int N, int K,
+                 long long ldc, void* stream) {
+    t_last_error.clear();
+    if (M < 0 || N < 0 || K <= 0) return fail(DT_ERR_INVALID_ARGUMENT, "need M, N >= 0 and K > 0");
+    if (c_mode < 0 || c_mode > 2) return fail(DT_ERR_INVALID_ARGUMENT, "c_mode must be 0 (store fp32), 1 (store bf16) or 2 (add fp32)");
+    if (M == 0 || N == 0) return DT_OK;
+    if ((!a_mn || !b_mn) && (K % 8) != 0) return fail(DT_ERR_INVALID_ARGUMENT, "K-major operands need K %% 8 == 0");
+    if ((a_mn && (M % 8) != 0) || (b_mn && (N % 8) != 0))
+        return fail(DT_ERR_INVALID_ARGUMENT, "an MN-major operand needs its M (or N) %% 8 == 0");
+    if (!A || !B || !C || !aligned16(A) || !aligned16(B) || !aligned16(C))
+        return fail(DT_ERR_INVALID_ARGUMENT, "A, B, C must be non-null and 16-byte aligned");
+    if (ldc < N || (ldc % (c_mode == 1 ? 8 : 4)) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ldc must be >= N and keep rows 16-byte aligned");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    return launch_gemm(A, B, C, c_mode == 1 ? 1 : 0, M, N, K, ldc, reinterpret_cast<cudaStream_t>(stream), 1,
+                       c_mode == 2 ? dt::gemm::kAccum : dt::gemm::kStore, nullptr, 0, 0, a_mn ? 1 : 0, b_mn ? 1 : 0);
+}
+
 int dt_gemm_bf16_tn_planar(const void* A, int a_planes, const void* B, void* C, int c_bf16, int M, int N, int K,
                            long long ldc, void* stream) {
     t_last_error.clear();
@@ -948,11 +980,13 @@ int dt_rope_tables(float* sin_out, float* cos_out, int max_seq, int head_dim, fl
 
 // ---- attention layer -------------------------------------------------------
 
+// The fp32 weights stay on the device as the master copy the training step
+// updates (the reference keeps fp32 param<2> members, param.h:5-15); the bf16
+// copies the tensor cores read are derived from it.
 static int attn_upload(dt_attn* a, const dt_attn_weights* w) {
     const int d = w->d_model;
     const size_t dd = (size_t)d * d;
-    float* stage = nullptr;
-    DT_CUDA(cudaMalloc(&stage, dd * 4));
+    DT_CUDA(cudaMalloc(&a->master, 4 * dd * 4));
     DT_CUDA(cudaMalloc(&a->wqkv, 3 * dd * 2));
     DT_CUDA(cudaMalloc(&a->wo, dd * 2));
     DT_CUDA(cudaMalloc(&a->qg, (size_t)d * 4));
@@ -960,11 +994,10 @@ static int attn_upload(dt_attn* a, const dt_attn_weights* w) {
     const float* src[4] = {w->q_proj, w->k_proj, w->v_proj, w->o_proj};
     __nv_bfloat16* dst[4] = {a->wqkv, a->wqkv + dd, a->wqkv + 2 * dd, a->wo};
     for (int i = 0; i < 4; ++i) {
-        DT_CUDA(cudaMemcpy(stage, src[i], dd * 4, cudaMemcpyHostToDevice));
-        DT_TRY(launch_cast(stage, dst[i], (long long)dd, nullptr));
-        DT_CUDA(cudaDeviceSynchronize());
+        DT_CUDA(cudaMemcpy(a->master + i * dd, src[i], dd * 4, cudaMemcpyHostToDevice));
+        DT_TRY(launch_cast(a->master + i * dd, dst[i], (long long)dd, nullptr));
     }
-    DT_CUDA(cudaFree(stage));
+    DT_CUDA(cudaDeviceSynchronize());
     DT_CUDA(cudaMemcpy(a->qg, w->q_norm, (size_t)d * 4, cudaMemcpyHostToDevice));
     DT_CUDA(cudaMemcpy(a->kg, w->k_norm, (size_t)d * 4, cudaMemcpyHostToDevice));
     return DT_OK;
@@ -1094,6 +1127,9 @@ int dt_attn_destroy(dt_attn* a) {
     cudaFree(a->kg);
     cudaFree(a->ws);
     cudaFree(a->io);
+    cudaFree(a->master);
+    cudaFree(a->grad);
+    cudaFree(a->bws);
     if (a->stream) cudaStreamDestroy(a->stream);
     cudaSetDevice(prev);
     delete a;
@@ -1101,7 +1137,10 @@ int dt_attn_destroy(dt_attn* a) {
 }
 
 // Scratch of attn_core for M tokens: [q|k|v] fp32 and four bf16 [M, d] arrays.
-static size_t attn_core_bytes(long long M) { return align256(M * 6144 * 4) + 4 * align256(M * 2048 * 2); }
+// [q|k|v] fp32, q/k/v/attention-output bf16, then softmax m and l ([M, 16] fp32 each)
+static size_t attn_core_bytes(long long M) {
+    return align256(M * 6144 * 4) + 4 * align256(M * 2048 * 2) + 2 * align256(M * 16 * 4);
+}
 
 // OlmoAttention::forward on a bf16 input (OlmoAttention.cpp:56-108): fused QKV
 // GEMM, QK-norm + RoPE prologue, flash attention, O projection into y (fp32).
@@ -1119,14 +1158,17 @@ static int attn_core(dt_attn* a, const void* xb, int B, int T, const int* seq_le
     void* kb = rest + act;
     void* vb = rest + 2 * act;
     void* ab = rest + 3 * act;
+    // the softmax statistics stay in the workspace for the backward
+    float* sm_m = reinterpret_cast<float*>(rest + 4 * act);
+    float* sm_l = reinterpret_cast<float*>(rest + 4 * act + align256(M * a->n_heads * 4));
     const float *sin_t, *cos_t;
     DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
     DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st, 1, dt::gemm::kStore, seq_lens, T,
                        0));                                                         // [q|k|v] = x Wqkv^T
     DT_TRY(launch_prologue(qkv, qkv + d, qkv + 2 * d, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
                            st));                                                    // norm + RoPE
-    DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, nullptr, nullptr, seq_lens, B, T, a->n_heads,
-                        1.0f / std::sqrt(128.0f), 1, st));                          // attention
+    DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, sm_m, sm_l, seq_lens, B, T, a->n_heads, 1.0f / std::sqrt(128.0f), 1,
+                        st));                                                       // attention
     DT_TRY(launch_gemm(ab, a->wo, y, 0, (int)M, d, d, d, st, 1, dt::gemm::kStore, seq_lens, T,
                        1));                                                         // y = a Wo^T
     return DT_OK;
@@ -1164,6 +1206,9 @@ int dt_attn_forward(dt_attn* a, const float* x, int B, int T, const int* seq_len
     DT_TRY(attn_workspace(a, M, &ws));
     void* xb = ws;
     DT_TRY(launch_cast(x, xb, M * d, st));  // x -> bf16
+    a->last_B = B;
+    a->last_T = T;
+    a->last_varlen = seq_lens != nullptr;
     return attn_core(a, xb, B, T, seq_lens, y, ws + align256(M * d * 2), dev, st);
 }
 
@@ -1198,6 +1243,186 @@ int dt_attn_forward_host(dt_attn* a, const float* x, int B, int T, const int* se
     return read_device_error(&had);
 }
 
+// ---- training path: OlmoAttention::backward / step / zero_grad --------------
+//
+// The forward leaves in the handle's workspace exactly the activations the
+// reference saves as members (OlmoAttention.h:28-38): bf16 x, the fp32 [q|k|v]
+// projections before the norm, the bf16 q/k/v after norm and RoPE, the bf16
+// attention output and the softmax statistics.  The backward of the last
+// forward (same B, T; no seq_lens) runs as
+//   dWo += dY^T A,  dA = dY Wo                       (OlmoAttention.cpp:194-209)
+//   dQ, dK, dV = flash backward(dA, A, m, l, q, k, v) (:211-225)
+//   RoPE^T and QK-RMSNorm backward -> [dq|dk|dv] bf16 (:227-237)
+//   d[Wq;Wk;Wv] += [dq|dk|dv]^T x,  dX = [dq|dk|dv] [Wq;Wk;Wv]  (:239-298)
+// with the gradients accumulated (beta = 1, as the reference) until zero_grad.
+
+static int attn_grads(dt_attn* a) {
+    if (a->grad) return DT_OK;
+    const size_t d = (size_t)a->d_model;
+    DT_CUDA(cudaMalloc(&a->grad, (4 * d * d + 2 * d) * 4));
+    DT_CUDA(cudaMemset(a->grad, 0, (4 * d * d + 2 * d) * 4));
+    return DT_OK;
+}
+
+int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void* stream) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (B != a->last_B || T != a->last_T || (long long)B * T == 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "backward needs the shape of the last forward (B=%d T=%d), got B=%d T=%d",
+                    a->last_B, a->last_T, B, T);
+    if (a->last_varlen)
+        return fail(DT_ERR_UNSUPPORTED, "backward of a forward with seq_lens (the reference has no padding mask)");
+    if (!dy || !dx || !aligned16(dy) || !aligned16(dx))
+        return fail(DT_ERR_INVALID_ARGUMENT, "dy/dx must be non-null and 16-byte aligned");
+    DT_CUDA(cudaSetDevice(a->device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    DT_TRY(attn_grads(a));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const long long M = (long long)B * T;
+    const int d = a->d_model, H = a->n_heads;
+    const size_t dd = (size_t)d * d;
+    // forward activations in the workspace (layout of dt_attn_forward / attn_core)
+    uint8_t* ws = reinterpret_cast<uint8_t*>(a->ws);
+    const void* xb = ws;
+    uint8_t* core = ws + align256(M * d * 2);
+    const float* qkv = reinterpret_cast<const float*>(core);
+    uint8_t* rest = core + align256(M * 3 * d * 4);
+    const size_t act = align256(M * d * 2);
+    const void *qb = rest, *kb = rest + act, *vb = rest + 2 * act, *ab = rest + 3 * act;
+    const float* sm_m = reinterpret_cast<const float*>(rest + 4 * act);
+    const float* sm_l = reinterpret_cast<const float*>(rest + 4 * act + align256(M * H * 4));
+    // scratch
+    const size_t f32 = align256(M * d * 4), rows = flash_bwd_rows_bytes(B, T, H);
+    const size_t need = act + f32 + act + 2 * rows + 3 * f32 + align256(M * 3 * d * 2);
+    if (a->bws_bytes < need) {
+        if (a->bws) DT_CUDA(cudaFree(a->bws));
+        a->bws = nullptr;
+        a->bws_bytes = 0;
+        DT_CUDA(cudaMalloc(&a->bws, need));
+        a->bws_bytes = need;
+    }
+    uint8_t* w = reinterpret_cast<uint8_t*>(a->bws);
+    void* dyb = w;
+    float* da = reinterpret_cast<float*>(w + act);
+    void* dob = w + act + f32;
+    float* dvec = reinterpret_cast<float*>(w + 2 * act + f32);
+    float* lse2 = reinterpret_cast<float*>(w + 2 * act + f32 + rows);
+    float* dq = reinterpret_cast<float*>(w + 2 * act + f32 + 2 * rows);
+    float* dk = dq + f32 / 4;
+    float* dv = dk + f32 / 4;
+    void* dqkv = w + 2 * act + 4 * f32 + 2 * rows;
+    float* g_qkv = a->grad;
+    float* g_o = a->grad + 3 * dd;
+    float* g_qn = a->grad + 4 * dd;
+    float* g_kn = g_qn + d;
+    DT_TRY(launch_cast(dy, dyb, M * d, st));
+    DT_TRY(launch_gemm(dyb, ab, g_o, 0, d, d, (int)M, d, st, 1, dt::gemm::kAccum, nullptr, 0, 0, 1, 1));  // dWo += dY^T A
+    DT_TRY(launch_gemm(dyb, a->wo, da, 0, (int)M, d, d, d, st, 1, dt::gemm::kStore, nullptr, 0, 0, 0, 1));  // dA = dY Wo
+    DT_TRY(launch_flash_bwd(qb, kb, vb, da, nullptr, ab, d, sm_m, sm_l, dq, dk, dv, B, T, H, 1.0f / std::sqrt(128.0f), 1,
+                            dob, dvec, lse2, st));
+    const float *sin_t, *cos_t;
+    DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
+    dt::elem::NormRopeBwdParams np{};
+    np.dq = dq;
+    np.dk = dk;
+    np.dv = dv;
+    np.xq = qkv;
+    np.xk = qkv + d;
+    np.ld_x = 3 * d;
+    np.q_gain = a->qg;
+    np.k_gain = a->kg;
+    np.sin_t = sin_t;
+    np.cos_t = cos_t;
+    np.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv);
+    np.dqg = g_qn;
+    np.dkg = g_kn;
+    np.M = M;
+    np.T = T;
+    np.eps = a->eps;
+    dt::elem::qk_norm_rope_bwd_kernel<<<(unsigned)((M + dt::elem::kBwdRows - 1) / dt::elem::kBwdRows),
+                                        dt::elem::kPrologueThreads, 0, st>>>(np);
+    DT_CUDA(cudaGetLastError());
+    DT_TRY(launch_gemm(dqkv, xb, g_qkv, 0, 3 * d, d, (int)M, d, st, 1, dt::gemm::kAccum, nullptr, 0, 0, 1,
+                       1));  // d[Wq;Wk;Wv] += [dq|dk|dv]^T x
+    DT_TRY(launch_gemm(dqkv, a->wqkv, dx, 0, (int)M, d, 3 * d, d, st, 1, dt::gemm::kStore, nullptr, 0, 0, 0,
+                       1));  // dX = [dq|dk|dv] [Wq;Wk;Wv]
+    return DT_OK;
+}
+
+int dt_attn_backward_host(dt_attn* a, const float* dy, int B, int T, float* dx) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (!dy || !dx) return fail(DT_ERR_INVALID_ARGUMENT, "null dy/dx");
+    const long long M = (long long)B * T;
+    if (M <= 0 || B != a->last_B || T != a->last_T)
+        return fail(DT_ERR_INVALID_ARGUMENT, "backward needs the shape of the last forward (B=%d T=%d)", a->last_B,
+                    a->last_T);
+    DT_CUDA(cudaSetDevice(a->device));
+    if (!a->stream) DT_CUDA(cudaStreamCreateWithFlags(&a->stream, cudaStreamNonBlocking));
+    const size_t xb = align256((size_t)M * a->d_model * 4);
+    if (a->io_bytes < 2 * xb) {
+        if (a->io) DT_CUDA(cudaFree(a->io));
+        a->io = nullptr;
+        a->io_bytes = 0;
+        DT_CUDA(cudaMalloc(&a->io, 2 * xb));
+        a->io_bytes = 2 * xb;
+    }
+    uint8_t* io = reinterpret_cast<uint8_t*>(a->io);
+    float* ddy = reinterpret_cast<float*>(io);
+    float* ddx = reinterpret_cast<float*>(io + xb);
+    DT_CUDA(cudaMemcpyAsync(ddy, dy, (size_t)M * a->d_model * 4, cudaMemcpyHostToDevice, a->stream));
+    DT_TRY(dt_attn_backward(a, ddy, B, T, ddx, a->stream));
+    DT_CUDA(cudaMemcpyAsync(dx, ddx, (size_t)M * a->d_model * 4, cudaMemcpyDeviceToHost, a->stream));
+    DT_CUDA(cudaStreamSynchronize(a->stream));
+    bool had;
+    return read_device_error(&had);
+}
+
+int dt_attn_step(dt_attn* a, float lr, void* stream) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    DT_CUDA(cudaSetDevice(a->device));
+    DT_TRY(attn_grads(a));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const long long dd = (long long)a->d_model * a->d_model;
+    dt::elem::sgd_kernel<<<148 * 8, 256, 0, st>>>(a->master, a->grad, a->wqkv, lr, 3 * dd);
+    dt::elem::sgd_kernel<<<148 * 8, 256, 0, st>>>(a->master + 3 * dd, a->grad + 3 * dd, a->wo, lr, dd);
+    dt::elem::sgd_kernel<<<8, 256, 0, st>>>(a->qg, a->grad + 4 * dd, nullptr, lr, a->d_model);
+    dt::elem::sgd_kernel<<<8, 256, 0, st>>>(a->kg, a->grad + 4 * dd + a->d_model, nullptr, lr, a->d_model);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int dt_attn_zero_grad(dt_attn* a, void* stream) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    DT_CUDA(cudaSetDevice(a->device));
+    if (!a->grad) return DT_OK;
+    const size_t d = (size_t)a->d_model;
+    DT_CUDA(cudaMemsetAsync(a->grad, 0, (4 * d * d + 2 * d) * 4, reinterpret_cast<cudaStream_t>(stream)));
+    return DT_OK;
+}
+
+int dt_attn_get_params_host(dt_attn* a, float* q_proj, float* k_proj, float* v_proj, float* o_proj, float* q_norm,
+                            float* k_norm, int gradients) {
+    t_last_error.clear();
+    if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    DT_CUDA(cudaSetDevice(a->device));
+    DT_CUDA(cudaDeviceSynchronize());
+    const size_t d = (size_t)a->d_model, dd = d * d;
+    if (gradients) DT_TRY(attn_grads(a));
+    const float* base = gradients ? a->grad : a->master;
+    float* outs[4] = {q_proj, k_proj, v_proj, o_proj};
+    for (int i = 0; i < 4; ++i)
+        if (outs[i]) DT_CUDA(cudaMemcpy(outs[i], base + i * dd, dd * 4, cudaMemcpyDeviceToHost));
+    const float* qn = gradients ? a->grad + 4 * dd : a->qg;
+    const float* kn = gradients ? a->grad + 4 * dd + d : a->kg;
+    if (q_norm) DT_CUDA(cudaMemcpy(q_norm, qn, d * 4, cudaMemcpyDeviceToHost));
+    if (k_norm) DT_CUDA(cudaMemcpy(k_norm, kn, d * 4, cudaMemcpyDeviceToHost));
+    bool had;
+    return read_device_error(&had);
+}
 
 // ---- full model prefill (configuration 3) ------------------------------------
 

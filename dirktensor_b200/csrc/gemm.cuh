@@ -25,6 +25,14 @@
 // an all-to-all delivers a token slice of the per-head attention outputs from
 // head-sharded ranks (plane = source rank), so the O projection reads it with a
 // 3-D tensor map instead of a repacking pass.
+// Either operand may instead be MN-major (a_mn / b_mn): stored [K, M] (or
+// [K, N]) row-major, i.e. the transposed product the training path needs --
+// dW = dY^T X and dX = dY W (OlmoAttention.cpp:201-205, 207, 250-267, 278-298)
+// read the row-major activations and weights directly.  An MN-major tile is two
+// (A) or BN/64 (B) 64-wide column strips of 64 K-rows each, loaded by 64 x 64
+// TMA boxes; the UMMA descriptor steps 16 K-rows (2 KB) per instruction with the
+// strips 8 KB apart.  Epilogue kAccum adds the product to an fp32 C (the
+// reference's beta = 1 gradient accumulation).
 #pragma once
 #include "dt_common.cuh"
 
@@ -61,6 +69,8 @@ struct Params {
     const int* seq_lens;
     int seq_T;
     int pad_zero;
+    int a_mn;           // 1: A stored [K, M] row-major (M contiguous)
+    int b_mn;           // 1: B stored [K, N] row-major (N contiguous)
 };
 
 // True when rows [m0, m0 + rows) all lie in one sequence's right padding.
@@ -70,7 +80,7 @@ __device__ __forceinline__ bool tile_is_padding(const Params& p, int m0) {
     return (m0 - b * p.seq_T) >= p.seq_lens[b];
 }
 
-enum Epilogue : int { kStore = 0, kSwiGLU = 1 };
+enum Epilogue : int { kStore = 0, kSwiGLU = 1, kAccum = 2 };
 
 template <int BN>
 struct __align__(1024) SmemT {
@@ -102,6 +112,13 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, c
                 w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
                 d[i] = w;
             }
+        } else if (p.epilogue == kAccum) {
+            float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + (long long)row * p.ldc + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 o = d[i];
+                d[i] = make_float4(o.x + v[4 * i], o.y + v[4 * i + 1], o.z + v[4 * i + 2], o.w + v[4 * i + 3]);
+            }
         } else {
             float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + (long long)row * p.ldc + col);
 #pragma unroll
@@ -113,6 +130,8 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, c
             if (col + e < p.N) {
                 if (p.c_bf16)
                     reinterpret_cast<__nv_bfloat16*>(p.C)[(long long)row * p.ldc + col + e] = __float2bfloat16_rn(v[e]);
+                else if (p.epilogue == kAccum)
+                    reinterpret_cast<float*>(p.C)[(long long)row * p.ldc + col + e] += v[e];
                 else
                     reinterpret_cast<float*>(p.C)[(long long)row * p.ldc + col + e] = v[e];
             }
@@ -170,13 +189,21 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     const int s = kit % kStages;
                     if (!mbar_wait(&sm.empty[s], ((kit / kStages) & 1) ^ 1, kSiteEmpty)) { ok = false; break; }
                     mbar_arrive_expect_tx(&sm.full[s], kABytes + kBBytes);
-                    if (p.a_plane_k) {
+                    if (p.a_mn) {
+                        for (int a = 0; a < kBM / 64; ++a)
+                            tma_load_2d(sm.a[s] + a * 8192, &tmap_a, &sm.full[s], m0 + 64 * a, kb * kBK);
+                    } else if (p.a_plane_k) {
                         const int plane = (kb * kBK) / p.a_plane_k;
                         tma_load_3d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK - plane * p.a_plane_k, m0, plane);
                     } else {
                         tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * kBK, m0);
                     }
-                    tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * kBK, n0);
+                    if (p.b_mn) {
+                        for (int a = 0; a < BN / 64; ++a)
+                            tma_load_2d(sm.b[s] + a * 8192, &tmap_b, &sm.full[s], n0 + 64 * a, kb * kBK);
+                    } else {
+                        tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * kBK, n0);
+                    }
                 }
             }
             if (!ok)  // drain copies still in flight before the CTA exits
@@ -186,7 +213,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     } else if (warp == 1) {
         // ------------------------------ MMA issuer --------------------------
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, 0, 0);
+            const uint32_t idesc = umma_idesc_bf16(kBM, BN, p.a_mn, p.b_mn);
             int kit = 0, it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
@@ -205,9 +232,13 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     const uint32_t a0 = smem_u32(sm.a[s]);
                     const uint32_t b0 = smem_u32(sm.b[s]);
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk)
-                        umma_ss(d, umma_desc_sw128(a0 + kk * 32, 16, 1024), umma_desc_sw128(b0 + kk * 32, 16, 1024),
-                                idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint64_t da = p.a_mn ? umma_desc_sw128(a0 + kk * 2048, 8192, 1024)
+                                                   : umma_desc_sw128(a0 + kk * 32, 16, 1024);
+                        const uint64_t db = p.b_mn ? umma_desc_sw128(b0 + kk * 2048, 8192, 1024)
+                                                   : umma_desc_sw128(b0 + kk * 32, 16, 1024);
+                        umma_ss(d, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
                     umma_commit(&sm.empty[s]);
                 }
                 if (ok) umma_commit(&sm.acc_full[acc]);

@@ -146,3 +146,154 @@ qk_norm_rope_kernel(const PrologueParams p) {
 
 }  // namespace elem
 }  // namespace dt
+
+namespace dt {
+namespace elem {
+
+// ---------------------------------------------------------------------------
+// Backward of QK-RMSNorm + RoPE (OlmoAttention.cpp:149-187 and :228-237,
+// RMSNorm.cpp:24-36), fused per token, plus the bf16 packing of dV:
+//   dn = RoPE^T(dq_rope)            d_in[d] = dy[d] c[d] + dy[d+64] s[d+64],
+//                                    d_in[d+64] = -dy[d] s[d] + dy[d+64] c[d+64]
+//   rms = sqrt(mean(x^2) + eps),  x_hat = x / rms,  y = x_hat * g
+//   c = mean(dn * y),  dx = (g * dn - x_hat * c) / rms,  dg += dn * x_hat
+// (x = the projection before the norm, which the forward left in its fp32
+// [q|k|v] buffer).  Writes dx of q and k and the bf16 dV into one
+// [M, 3*2048] bf16 row (the operand of the projection-gradient GEMMs) and
+// adds the gain gradients into dqg / dkg.  A CTA of 256 threads walks
+// kBwdRows tokens with the forward's thread layout (thread = 4 RoPE pairs of
+// one head), keeping its gain-gradient partial sums in registers.
+// ---------------------------------------------------------------------------
+constexpr int kBwdRows = 32;
+
+struct NormRopeBwdParams {
+    const float* dq;      // [M, 2048] gradient of the RoPE'd q
+    const float* dk;      // [M, 2048]
+    const float* dv;      // [M, 2048]
+    const float* xq;      // pre-norm q, row stride ld_x
+    const float* xk;      // pre-norm k
+    long long ld_x;
+    const float* q_gain;
+    const float* k_gain;
+    const float* sin_t;
+    const float* cos_t;
+    __nv_bfloat16* dqkv;  // [M, 3*2048]
+    float* dqg;           // [2048], accumulated
+    float* dkg;           // [2048], accumulated
+    long long M;
+    int T;
+    float eps;
+};
+
+__global__ void __launch_bounds__(kPrologueThreads)
+qk_norm_rope_bwd_kernel(const NormRopeBwdParams p) {
+    __shared__ float red[4][kPrologueThreads / 32];
+    const int h = threadIdx.x >> 4;
+    const int j = threadIdx.x & 15;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int d_lo = h * kHeadDim + 4 * j;
+    const int d_hi = d_lo + 64;
+    const float4 gq_lo = *reinterpret_cast<const float4*>(p.q_gain + d_lo);
+    const float4 gq_hi = *reinterpret_cast<const float4*>(p.q_gain + d_hi);
+    const float4 gk_lo = *reinterpret_cast<const float4*>(p.k_gain + d_lo);
+    const float4 gk_hi = *reinterpret_cast<const float4*>(p.k_gain + d_hi);
+    float accq[8], acck[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) accq[i] = acck[i] = 0.f;
+    const long long r0 = (long long)blockIdx.x * kBwdRows;
+    for (int rr = 0; rr < kBwdRows; ++rr) {
+        const long long row = r0 + rr;
+        if (row >= p.M) break;  // uniform across the CTA
+        const int t = static_cast<int>(row % p.T);
+        const float4 c_lo = *reinterpret_cast<const float4*>(p.cos_t + (long long)t * kHeadDim + 4 * j);
+        const float4 c_hi = *reinterpret_cast<const float4*>(p.cos_t + (long long)t * kHeadDim + 4 * j + 64);
+        const float4 s_lo = *reinterpret_cast<const float4*>(p.sin_t + (long long)t * kHeadDim + 4 * j);
+        const float4 s_hi = *reinterpret_cast<const float4*>(p.sin_t + (long long)t * kHeadDim + 4 * j + 64);
+        float dn[2][8], xv[2][8];
+        const float* dsrc[2] = {p.dq + row * kDModel, p.dk + row * kDModel};
+        const float* xsrc[2] = {p.xq + row * p.ld_x, p.xk + row * p.ld_x};
+        float part[4] = {0.f, 0.f, 0.f, 0.f};  // sum x^2 (q, k), sum dn*x*g (q, k)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const float4 ylo = *reinterpret_cast<const float4*>(dsrc[u] + d_lo);
+            const float4 yhi = *reinterpret_cast<const float4*>(dsrc[u] + d_hi);
+            const float4 xlo = *reinterpret_cast<const float4*>(xsrc[u] + d_lo);
+            const float4 xhi = *reinterpret_cast<const float4*>(xsrc[u] + d_hi);
+            const float yl[4] = {ylo.x, ylo.y, ylo.z, ylo.w}, yh[4] = {yhi.x, yhi.y, yhi.z, yhi.w};
+            const float cl[4] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w}, ch[4] = {c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+            const float sl[4] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w}, sh[4] = {s_hi.x, s_hi.y, s_hi.z, s_hi.w};
+            const float4 glo = u ? gk_lo : gq_lo, ghi = u ? gk_hi : gq_hi;
+            const float gl[4] = {glo.x, glo.y, glo.z, glo.w}, gh[4] = {ghi.x, ghi.y, ghi.z, ghi.w};
+            xv[u][0] = xlo.x; xv[u][1] = xlo.y; xv[u][2] = xlo.z; xv[u][3] = xlo.w;
+            xv[u][4] = xhi.x; xv[u][5] = xhi.y; xv[u][6] = xhi.z; xv[u][7] = xhi.w;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                dn[u][e] = yl[e] * cl[e] + yh[e] * sh[e];
+                dn[u][4 + e] = -yl[e] * sl[e] + yh[e] * ch[e];
+                part[u] += xv[u][e] * xv[u][e] + xv[u][4 + e] * xv[u][4 + e];
+                part[2 + u] += dn[u][e] * xv[u][e] * gl[e] + dn[u][4 + e] * xv[u][4 + e] * gh[e];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) part[k] += __shfl_xor_sync(0xffffffffu, part[k], o);
+            if (lane == 0) red[k][wid] = part[k];
+        }
+        __syncthreads();
+        float tot[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float s = 0.f;
+#pragma unroll
+            for (int w = 0; w < kPrologueThreads / 32; ++w) s += red[k][w];
+            tot[k] = s;
+        }
+        __syncthreads();  // `red` is rewritten by the next row
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const float rms = sqrtf(tot[u] / (float)kDModel + p.eps);
+            const float c = tot[2 + u] / rms / (float)kDModel;  // mean(dn * y), y = x / rms * g
+            const float4 glo = u ? gk_lo : gq_lo, ghi = u ? gk_hi : gq_hi;
+            const float g8[8] = {glo.x, glo.y, glo.z, glo.w, ghi.x, ghi.y, ghi.z, ghi.w};
+            float dx[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float xh = xv[u][e] / rms;
+                dx[e] = (g8[e] * dn[u][e] - xh * c) / rms;
+                if (u) acck[e] += dn[u][e] * xh;
+                else accq[e] += dn[u][e] * xh;
+            }
+            __nv_bfloat16* out = p.dqkv + row * (3 * kDModel) + u * kDModel;
+            *reinterpret_cast<uint2*>(out + d_lo) = make_uint2(pack_bf16x2(dx[0], dx[1]), pack_bf16x2(dx[2], dx[3]));
+            *reinterpret_cast<uint2*>(out + d_hi) = make_uint2(pack_bf16x2(dx[4], dx[5]), pack_bf16x2(dx[6], dx[7]));
+        }
+        // dV: 8 consecutive elements per thread
+        const float4 va = *reinterpret_cast<const float4*>(p.dv + row * kDModel + 8 * threadIdx.x);
+        const float4 vb = *reinterpret_cast<const float4*>(p.dv + row * kDModel + 8 * threadIdx.x + 4);
+        *reinterpret_cast<uint4*>(p.dqkv + row * (3 * kDModel) + 2 * kDModel + 8 * threadIdx.x) =
+            make_uint4(pack_bf16x2(va.x, va.y), pack_bf16x2(va.z, va.w), pack_bf16x2(vb.x, vb.y),
+                       pack_bf16x2(vb.z, vb.w));
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        atomicAdd(p.dqg + d_lo + e, accq[e]);
+        atomicAdd(p.dqg + d_hi + e, accq[4 + e]);
+        atomicAdd(p.dkg + d_lo + e, acck[e]);
+        atomicAdd(p.dkg + d_hi + e, acck[4 + e]);
+    }
+}
+
+// SGD step (OlmoAttention.cpp:315-322, RMSNorm.cpp:38-41): w -= lr * g on the
+// fp32 master weights, and optionally refresh their bf16 working copy.
+__global__ void sgd_kernel(float* __restrict__ w, const float* __restrict__ g, __nv_bfloat16* __restrict__ wb,
+                           float lr, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float v = w[i] - lr * g[i];
+        w[i] = v;
+        if (wb) wb[i] = __float2bfloat16_rn(v);
+    }
+}
+
+}  // namespace elem
+}  // namespace dt

@@ -162,6 +162,22 @@ int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_a
 int dt_attn_forward(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y, void* stream);
 /* Same with host buffers; seq_lens is a host int[B] or NULL. */
 int dt_attn_forward_host(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y);
+/* Training path of the layer (OlmoAttention::backward / step / zero_grad,
+ * OlmoAttention.cpp:189-330, RMSNorm.cpp:24-41).  dt_attn_backward takes the
+ * gradient dy of the last dt_attn_forward's output (same B, T; that forward
+ * without seq_lens), writes dx (fp32 [B, T, d_model] device array) and adds the
+ * weight gradients into the handle's fp32 gradient buffers (Wq, Wk, Wv, Wo,
+ * q_norm, k_norm), which start at zero and are cleared by dt_attn_zero_grad.
+ * dt_attn_step applies w -= lr * grad to the fp32 master weights (kept on the
+ * device since creation) and refreshes the bf16 copies the kernels read.
+ * dt_attn_get_params_host copies the weights (gradients = 0) or the gradients
+ * (gradients = 1) to host arrays (nulls skipped), after a device sync. */
+int dt_attn_backward(dt_attn* attn, const float* dy, int B, int T, float* dx, void* stream);
+int dt_attn_backward_host(dt_attn* attn, const float* dy, int B, int T, float* dx);
+int dt_attn_step(dt_attn* attn, float lr, void* stream);
+int dt_attn_zero_grad(dt_attn* attn, void* stream);
+int dt_attn_get_params_host(dt_attn* attn, float* q_proj, float* k_proj, float* v_proj, float* o_proj, float* q_norm,
+                            float* k_norm, int gradients);
 int dt_attn_destroy(dt_attn* attn);
 
 /* ---- full model prefill (configuration 3) -------------------------------
@@ -220,6 +236,15 @@ int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream);
  * The projection products of OlmoAttention.cpp:68,74,80,103-105. */
 int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, int N, int K, long long ldc,
                     void* stream);
+/* General form: C (+)= op(A) . op(B)^T with bf16 operands.  a_mn = 0: A is
+ * [M, K] row-major; a_mn = 1: A is stored [K, M] row-major (the transposed
+ * operand).  b_mn = 0: B is [N, K]; b_mn = 1: B is stored [K, N].  c_mode: 0
+ * store fp32, 1 store bf16, 2 add into an fp32 C.  Replaces the training
+ * path's sgemm calls: dW += dY^T X (OlmoAttention.cpp:201-205, 250-267; a_mn =
+ * b_mn = 1, c_mode = 2) and dX = dY W (:207, 278-298; b_mn = 1).  An MN-major
+ * operand needs its M (or N) to be a multiple of 8. */
+int dt_gemm_bf16(const void* A, int a_mn, const void* B, int b_mn, void* C, int c_mode, int M, int N, int K,
+                 long long ldc, void* stream);
 /* The same product with a planar A: a_planes arrays [M, K/a_planes] stored
  * back to back (A[m, p*(K/a_planes) + x] = plane_p[m, x]); K/a_planes must be a
  * multiple of 64.  This is the O projection (OlmoAttention.cpp:103-105) of the

@@ -15,6 +15,7 @@ TOL_L_REL = 2e-2          # softmax_l, relative
 TOL_LAYER_REL_L2 = 1.5e-2  # attention layer output y, relative L2
 TOL_GEMM_REL_L2 = 1e-5    # GEMM vs fp32 matmul of the same bf16-rounded operands
 TOL_BWD_REL_L2 = 2e-2    # attention gradients dQ, dK, dV, relative L2 (bf16 Q/K/V/dO/P/dS operands)
+TOL_LAYER_BWD_REL_L2 = 3e-2  # layer backward: dx and the six weight gradients, relative L2
 
 
 def randn(seed: int, shape, scale: float = 1.0) -> np.ndarray:

@@ -3,9 +3,13 @@
 // OlmoBlock-like owner holding OlmoAttention by value (OlmoBlock.h:19) that
 // constructs it from (folder, index) and calls forward (OlmoBlock.cpp:6,14).
 //
-//   test_dropin flash <dir> B T H     reads dir/{q,k,v}.f32, writes dir/{o,m,l}.f32
+//   test_dropin flash <dir> B T H     reads dir/{q,k,v,do}.f32, writes dir/{o,m,l}.f32 and
+//                                     flash_attention_backward's dir/{dq,dk,dv}.f32
 //   test_dropin layer <dir> index B T reads dir/x.f32 and the layer's .npy weights
 //                                     from dir, writes dir/y.f32
+//   test_dropin train <dir> index B T reads dir/{x,dy}.f32: forward, backward (writes dir/dx.f32),
+//                                     step(1e-3), forward again (writes dir/y2.f32), zero_grad
+//                                     -- the OlmoBlock calls (OlmoBlock.cpp:14,28,33,40)
 //   test_dropin model <dir> L B T     reads dir/ids.u32 and an L-layer checkpoint from
 //                                     dir, writes dir/logits.f32 (OlmoModel)
 #include <cstdio>
@@ -36,6 +40,9 @@ struct BlockLike {
     OlmoAttention m_attention;
     BlockLike(const std::string& folder, unsigned index) : m_attention(folder, index) {}
     xt::xtensor<float, 3> forward(const xt::xtensor<float, 3>& x) { return m_attention.forward(x); }
+    xt::xtensor<float, 3> backward(const xt::xtensor<float, 3>& d) { return m_attention.backward(d); }
+    void step(float lr) { m_attention.step(lr); }
+    void zero_grad() { m_attention.zero_grad(); }
 };
 
 int main(int argc, char** argv) {
@@ -54,11 +61,13 @@ int main(int argc, char** argv) {
             write_from(dir + "/o.f32", r.output);
             write_from(dir + "/m.f32", r.softmax_m);
             write_from(dir + "/l.f32", r.softmax_l);
-            try {
-                flash_attention_backward(r.output, r.output, r.softmax_m, r.softmax_l, q, k, v, 0.1f);
-                return 3;  // must not succeed
-            } catch (const std::logic_error&) {
-            }
+            xt::xtensor<float, 4> d_out = xt::empty<float>({B, T, H, std::size_t(128)});
+            read_into(dir + "/do.f32", d_out);
+            const FlashAttentionGradients g = flash_attention_backward(d_out, r.output, r.softmax_m, r.softmax_l, q,
+                                                                       k, v, 1.0f / 11.313708498984761f, true);
+            write_from(dir + "/dq.f32", g.d_Q);
+            write_from(dir + "/dk.f32", g.d_K);
+            write_from(dir + "/dv.f32", g.d_V);
         } else if (mode == "layer" && argc == 6) {
             const unsigned index = static_cast<unsigned>(std::stoul(argv[3]));
             const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);
@@ -69,6 +78,19 @@ int main(int argc, char** argv) {
             const xt::xtensor<float, 3> y = moved.forward(x);
             write_from(dir + "/y.f32", y);
             moved.m_attention.zero_grad();
+        } else if (mode == "train" && argc == 6) {
+            const unsigned index = static_cast<unsigned>(std::stoul(argv[3]));
+            const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);
+            xt::xtensor<float, 3> x = xt::empty<float>({B, T, std::size_t(2048)});
+            xt::xtensor<float, 3> dy = xt::empty<float>({B, T, std::size_t(2048)});
+            read_into(dir + "/x.f32", x);
+            read_into(dir + "/dy.f32", dy);
+            BlockLike block(dir, index);
+            block.forward(x);
+            write_from(dir + "/dx.f32", block.backward(dy));
+            block.step(1e-3f);
+            write_from(dir + "/y2.f32", block.forward(x));
+            block.zero_grad();
         } else if (mode == "model" && argc == 6) {
             const unsigned layers = static_cast<unsigned>(std::stoul(argv[3]));
             const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);

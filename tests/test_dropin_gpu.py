@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 
 import oracle
-from common import SCALE, TOL_ATTN_REL_L2, TOL_LAYER_REL_L2, layer_weights, qkv, randn, rel_l2
+from common import (SCALE, TOL_ATTN_REL_L2, TOL_BWD_REL_L2, TOL_LAYER_BWD_REL_L2, TOL_LAYER_REL_L2,
+                    layer_weights, qkv, randn, rel_l2)
 
 pytestmark = pytest.mark.gpu
 
@@ -29,7 +30,8 @@ def dropin_bin(tmp_path_factory):
 def test_dropin_flash_attention_forward(cuda, dropin_bin, tmp_path):
     B, T, H = 2, 300, 4
     q, k, v = qkv(31, B, T, H)
-    for n, a in (("q", q), ("k", k), ("v", v)):
+    do = randn(32, q.shape)
+    for n, a in (("q", q), ("k", k), ("v", v), ("do", do)):
         a.tofile(tmp_path / f"{n}.f32")
     subprocess.run([dropin_bin, "flash", str(tmp_path), str(B), str(T), str(H)], check=True)
     o = np.fromfile(tmp_path / "o.f32", np.float32).reshape(B, T, H, 128)
@@ -37,6 +39,12 @@ def test_dropin_flash_attention_forward(cuda, dropin_bin, tmp_path):
     ro, rm, rl = oracle.flash_fwd(q, k, v, SCALE, True)
     assert rel_l2(o, ro) < TOL_ATTN_REL_L2
     assert np.max(np.abs(m - rm)) < 5e-2
+    # flash_attention_backward through the drop-in (on the drop-in's own forward outputs)
+    l = np.fromfile(tmp_path / "l.f32", np.float32).reshape(B, T, H)
+    ref = oracle.flash_bwd(do, o, m, l, q, k, v, SCALE, True)
+    for n, r in zip(("dq", "dk", "dv"), ref):
+        got = np.fromfile(tmp_path / f"{n}.f32", np.float32).reshape(B, T, H, 128)
+        assert rel_l2(got, r) < TOL_BWD_REL_L2, n
 
 
 def test_dropin_olmo_attention_block_usage(cuda, dropin_bin, tmp_path):
@@ -53,6 +61,27 @@ def test_dropin_olmo_attention_block_usage(cuda, dropin_bin, tmp_path):
     # a missing layer surfaces as a C++ exception -> non-zero exit
     r = subprocess.run([dropin_bin, "layer", str(tmp_path), "6", str(B), str(T)], capture_output=True, text=True)
     assert r.returncode == 1 and "cannot open" in r.stderr
+
+
+def test_dropin_olmo_attention_training_calls(cuda, dropin_bin, tmp_path):
+    """forward -> backward -> step -> forward, as OlmoBlock drives it (OlmoBlock.cpp:14,28,33)."""
+    ws = layer_weights(34)
+    for n, w in zip(["q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"], ws):
+        np.save(tmp_path / f"model.layers.2.self_attn.{n}.weight.npy", w)
+    B, T = 1, 100
+    x = randn(35, (B, T, 2048))
+    dy = randn(36, (B, T, 2048))
+    x.tofile(tmp_path / "x.f32")
+    dy.tofile(tmp_path / "dy.f32")
+    subprocess.run([dropin_bin, "train", str(tmp_path), "2", str(B), str(T)], check=True)
+    dx = np.fromfile(tmp_path / "dx.f32", np.float32).reshape(B, T, 2048)
+    y2 = np.fromfile(tmp_path / "y2.f32", np.float32).reshape(B, T, 2048)
+    _, saved = oracle.attention_layer_train(x, *ws)
+    rdx, g = oracle.attention_layer_backward(dy, saved, *ws)
+    assert rel_l2(dx, rdx) < TOL_LAYER_BWD_REL_L2
+    keys = ["q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"]
+    stepped = [w - np.float32(1e-3) * g[k] for w, k in zip(ws, keys)]
+    assert rel_l2(y2, oracle.attention_layer(x, *stepped)) < TOL_LAYER_REL_L2
 
 
 def test_dropin_olmo_model(cuda, dropin_bin, tmp_path):

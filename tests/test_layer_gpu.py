@@ -28,6 +28,32 @@ def test_gemm_vs_torch_fp32(cuda, M, N, K):
     assert rel_l2(cb.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 1), (1, 1), (1, 0)])
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 1000), (6144, 2048, 520), (256, 384, 64), (136, 200, 300),
+                                   (1000, 2048, 2048)])
+def test_gemm_transposed_operands_vs_torch_fp32(cuda, a_mn, b_mn, M, N, K):
+    """The training path's products: dW = dY^T X (both operands MN-major, added
+    into the gradient) and dX = dY W (B MN-major)."""
+    import torch
+
+    import dirktensor_b200 as dt
+
+    if (a_mn and M % 8) or (b_mn and N % 8) or ((not a_mn or not b_mn) and K % 8):
+        pytest.skip("shape not supported by this operand layout")
+    a = torch.from_numpy(randn(M + K, (M, K))).to(cuda).to(torch.bfloat16)
+    b = torch.from_numpy(randn(N + K, (N, K), 0.05)).to(cuda).to(torch.bfloat16)
+    a_in = a.t().contiguous() if a_mn else a
+    b_in = b.t().contiguous() if b_mn else b
+    ref = a.float() @ b.float().t()
+    c = dt.gemm_bf16(a_in, b_in, a_mn=bool(a_mn), b_mn=bool(b_mn))
+    base = torch.from_numpy(randn(7, (M, N))).to(cuda)
+    acc = base.clone()
+    dt.gemm_bf16(a_in, b_in, a_mn=bool(a_mn), b_mn=bool(b_mn), out=acc, accumulate=True)
+    dt.check_device_error()
+    assert rel_l2(c.cpu().numpy(), ref.cpu().numpy()) < TOL_GEMM_REL_L2
+    assert rel_l2(acc.cpu().numpy(), (base + ref).cpu().numpy()) < TOL_GEMM_REL_L2
+
+
 def test_cast_is_round_to_nearest_even(cuda):
     import torch
 
