@@ -202,7 +202,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1: fused flash + NVLink stores (default) or an NCCL all-to-all")
-    ap.add_argument("--case", default=None, choices=["flash_bf16", "layer", "gemm"],
+    ap.add_argument("--case", default=None, choices=["flash_bf16", "flash_bwd", "layer", "gemm"],
                     help="profiling case for ncu: a few launches of one stage, no timing")
     ap.add_argument("--sweep", action="store_true",
                     help="config-1 sweep (T = 64 ... 6144) and config 4: flash kernel TFLOP/s per shape")
@@ -318,8 +318,10 @@ def main():
 
     layers = None
     model3 = None
+    train = None
     if world == 1:
         layers = bench_layers(torch, dt, dev, args)
+        train = bench_train(torch, dt, dev, args)
         if not args.no_model:
             model3 = bench_model(torch, dt, dev, args)
 
@@ -372,6 +374,7 @@ def main():
             "config1_t4096": t4096,
             "layers": layers,
             "model_config3": model3,
+            "training": train,
         }
         print(json.dumps(line), flush=True)
     hp.close()
@@ -468,6 +471,71 @@ def bench_model(torch, dt, dev, args):
     return {"B": Bm, "T": Tm, "n_layers": nl, "vocab": vocab, "ms": ms, "tok_s": tokens / (ms * 1e-3),
             "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "logits_finite": finite,
             "data": "synthetic ids, random N(0,0.02) weights"}
+
+
+def bench_train(torch, dt, dev, args):
+    """Training path (OlmoAttention::backward, flash_attention_backward).
+    flash_bwd: dt_flash_bwd (fp32 in/out, bf16 casts inside) at config 1
+    T=4096 (B=1) and at B=4, T=4096, H=16; algorithmic FLOPs 2.5x the causal
+    forward (5 products of the forward's 2), L2 flushed before each call.
+    layer: one attention layer forward + backward + SGD step at config 0 (B=1,
+    T=512) and at the config-3 layer shape (B=4, T=4096); FLOPs = forward
+    (2*tok*2048*8192 + 2*B*H*T^2*D) + backward (2x the projections + 2.5x the
+    attention)."""
+    out = {}
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    reps = max(3, min(args.steps, 10))
+    for name, Bt, Tt in (("flash_bwd_config1_t4096", 1, 4096), ("flash_bwd_b4_t4096", 4, 4096)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(Tt + Bt)
+        q, k, v, do = (torch.randn((Bt, Tt, H, D), generator=g, device=dev) for _ in range(4))
+        fwd = dt.flash_attention_forward(q, k, v, SCALE, True)
+        ts = []
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            dt.flash_attention_backward(do, fwd.output, fwd.softmax_m, fwd.softmax_l, q, k, v, SCALE, True)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        dt.check_device_error()
+        ms = statistics.median(ts)
+        f = 2.5 * 2.0 * Bt * H * Tt * Tt * D
+        out[name] = {"B": Bt, "T": Tt, "ms": ms, "flops": f, "tflops": f / (ms * 1e-3) / 1e12,
+                     "note": "includes the fp32->bf16 casts of q, k, v and dO"}
+    rng = np.random.default_rng(3)
+    w = [(0.02 * rng.standard_normal((DM, DM), dtype=np.float32)) for _ in range(4)]
+    gains = [(1 + 0.02 * rng.standard_normal(DM, dtype=np.float32)).astype(np.float32) for _ in range(2)]
+    attn = dt.OlmoAttention.from_weights(*w, *gains, device=dev.index or 0)
+    for name, Bl, Tl in (("layer_train_config0", 1, 512), ("layer_train_b4_t4096", 4, 4096)):
+        x = torch.from_numpy(rng.standard_normal((Bl, Tl, DM), dtype=np.float32)).to(dev)
+        dy = torch.from_numpy(0.01 * rng.standard_normal((Bl, Tl, DM), dtype=np.float32)).to(dev)
+        y, dx = torch.empty_like(x), torch.empty_like(x)
+        ts = []
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            attn.forward(x, out=y)
+            attn.backward(dy, out=dx)
+            attn.step(1e-6)
+            attn.zero_grad()
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        dt.check_device_error()
+        ms = statistics.median(ts)
+        tok = Bl * Tl
+        f_proj = 2.0 * tok * DM * 8192
+        f_attn = 2.0 * Bl * H * Tl * Tl * D
+        f = f_proj + f_attn + 2 * f_proj + 2.5 * f_attn
+        out[name] = {"B": Bl, "T": Tl, "ms": ms, "tok_s": tok / (ms * 1e-3), "flops": f,
+                     "tflops": f / (ms * 1e-3) / 1e12, "step": "forward + backward + SGD step + zero_grad"}
+    attn.close()
+    return out
 
 
 def bench_t4096(torch, dt, dev, args):
@@ -627,6 +695,11 @@ def run_case(args):
         c = torch.empty((M, N), dtype=torch.float32, device=dev)
         for _ in range(3):
             dt.gemm_bf16_tn(a, b, out=c)
+    elif args.case == "flash_bwd":
+        q, k, v, do = (torch.randn((Bc, Tc, H, D), generator=g, device=dev) for _ in range(4))
+        fwd = dt.flash_attention_forward(q, k, v, SCALE, True)
+        for _ in range(3):
+            dt.flash_attention_backward(do, fwd.output, fwd.softmax_m, fwd.softmax_l, q, k, v, SCALE, True)
     elif args.case == "flash_bf16":
         q, k, v = (torch.randn((Bc, Tc, H, D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
         out = torch.empty((Bc, Tc, H, D), device=dev)

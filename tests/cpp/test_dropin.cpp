@@ -10,6 +10,9 @@
 //   test_dropin train <dir> index B T reads dir/{x,dy}.f32: forward, backward (writes dir/dx.f32),
 //                                     step(1e-3), forward again (writes dir/y2.f32), zero_grad
 //                                     -- the OlmoBlock calls (OlmoBlock.cpp:14,28,33,40)
+//   test_dropin tokens <dir> <vocab> <file>...  token_batch of the files padded with the
+//                                     vocab's <|pad|> id (main.cpp:14-58): writes
+//                                     dir/batch.u32, prints "rows cols pad"
 //   test_dropin model <dir> L B T     reads dir/ids.u32 and an L-layer checkpoint from
 //                                     dir, writes dir/logits.f32 (OlmoModel)
 #include <cstdio>
@@ -18,10 +21,12 @@
 #include <iostream>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "FlashAttention.h"
 #include "OlmoAttention.h"
 #include "OlmoModel.h"
+#include "Tokens.h"
 
 template <class X>
 static void read_into(const std::string& path, X& x) {
@@ -91,6 +96,13 @@ int main(int argc, char** argv) {
             block.step(1e-3f);
             write_from(dir + "/y2.f32", block.forward(x));
             block.zero_grad();
+        } else if (mode == "tokens" && argc >= 5) {
+            const uint32_t pad = pad_token_id(argv[3]);
+            std::vector<std::string> files(argv + 4, argv + argc);
+            const xt::xtensor<uint32_t, 2> batch = token_batch(files, pad);
+            std::ofstream f(dir + "/batch.u32", std::ios::binary);
+            f.write(reinterpret_cast<const char*>(batch.data()), static_cast<std::streamsize>(batch.size() * 4));
+            std::cout << batch.shape(0) << " " << batch.shape(1) << " " << pad << "\n";
         } else if (mode == "model" && argc == 6) {
             const unsigned layers = static_cast<unsigned>(std::stoul(argv[3]));
             const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);
