@@ -462,7 +462,9 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
         p.pad_zero = pad_zero;
     }
     p.tiles_n = (N + bn - 1) / bn;
-    const long long tiles = (long long)p.tiles_n * ((M + dt::gemm::kBM - 1) / dt::gemm::kBM);
+    p.tiles_m = (M + dt::gemm::kBM - 1) / dt::gemm::kBM;
+    p.m_fastest = N > M ? 1 : 0;
+    const long long tiles = (long long)p.tiles_n * p.tiles_m;
     if (tiles > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "GEMM too large");
     p.num_tiles = (int)tiles;
     int dev = 0;
@@ -471,7 +473,8 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     if (pair) {
         // cluster tiles of 256 x 256 on SM pairs; persistent: one CTA per SM
         p.tiles_n = (N + dt::gemm2::kBN - 1) / dt::gemm2::kBN;
-        p.num_tiles = p.tiles_n * ((M + dt::gemm2::kBM - 1) / dt::gemm2::kBM);
+        p.tiles_m = (M + dt::gemm2::kBM - 1) / dt::gemm2::kBM;
+        p.num_tiles = p.tiles_n * p.tiles_m;
         const int clusters = std::max(1, std::min(p.num_tiles, sms / 2));
         dt::gemm2::gemm_bf16_tn_2sm_kernel<<<2 * clusters, dt::gemm2::kThreads, kGemm2Smem, st>>>(ma, mb, p);
         DT_CUDA(cudaGetLastError());

@@ -7,8 +7,7 @@
 // layout, which is exactly a K-major B operand, so no transpose is needed.
 //
 // Persistent kernel: one CTA per SM walks the 128 x 256 output tiles
-// (tile t, t + gridDim.x, ...; N varies fastest so the CTAs of one wave share
-// their A row panels in L2).  A 4-stage TMA ring (48 KB per stage) feeds one
+// (tile t, t + gridDim.x, ...; in the order tile_m / tile_n give, below).
 // 128x256x16 tcgen05.mma per 16-wide K step.  Two accumulators of 256 TMEM
 // columns alternate between tiles, so the epilogue of tile i (TMEM ->
 // registers -> global) runs while the MMAs of tile i+1 proceed.
@@ -71,7 +70,17 @@ struct Params {
     int pad_zero;
     int a_mn;           // 1: A stored [K, M] row-major (M contiguous)
     int b_mn;           // 1: B stored [K, N] row-major (N contiguous)
+    int tiles_m;        // ceil(M / tile rows)
+    int m_fastest;      // tile order: 0 = N varies fastest, 1 = M varies fastest
 };
+
+// Tile t's (row-tile, column-tile) in the persistent walk.  The order keeps the
+// larger operand's panel fixed while consecutive CTAs sweep the smaller one
+// (which then stays in L2): with N fastest, the CTAs of a wave share one A row
+// panel and B is re-read per row band; with M fastest (chosen when N > M, e.g.
+// the LM head's 100352 x 2048 weight), they share one B panel and read it once.
+__device__ __forceinline__ int tile_m(const Params& p, int t) { return p.m_fastest ? t % p.tiles_m : t / p.tiles_n; }
+__device__ __forceinline__ int tile_n(const Params& p, int t) { return p.m_fastest ? t / p.tiles_m : t % p.tiles_n; }
 
 // True when rows [m0, m0 + rows) all lie in one sequence's right padding.
 __device__ __forceinline__ bool tile_is_padding(const Params& p, int m0) {
@@ -182,8 +191,8 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             int kit = 0;  // k-blocks issued by this CTA (ring position)
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                const int m0 = (t / p.tiles_n) * kBM;
-                const int n0 = (t % p.tiles_n) * BN;
+                const int m0 = tile_m(p, t) * kBM;
+                const int n0 = tile_n(p, t) * BN;
                 if (tile_is_padding(p, m0)) continue;
                 for (int kb = 0; kb < nk; ++kb, ++kit) {
                     const int s = kit % kStages;
@@ -217,7 +226,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             int kit = 0, it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-                if (tile_is_padding(p, (t / p.tiles_n) * kBM)) continue;
+                if (tile_is_padding(p, tile_m(p, t) * kBM)) continue;
                 const int acc = it & 1;
                 const uint32_t empty_phase = ((it >> 1) & 1) ^ 1;
                 ++it;
@@ -253,9 +262,9 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int it = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-            const int row = (t / p.tiles_n) * kBM + q * 32 + lane;
-            const int n0 = (t % p.tiles_n) * BN;
-            if (tile_is_padding(p, (t / p.tiles_n) * kBM)) {
+            const int row = tile_m(p, t) * kBM + q * 32 + lane;
+            const int n0 = tile_n(p, t) * BN;
+            if (tile_is_padding(p, tile_m(p, t) * kBM)) {
                 if (p.pad_zero && p.epilogue == kStore) {
                     float z[32];
 #pragma unroll
@@ -272,7 +281,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             tc_fence_after();
             const uint32_t taddr = tmem + lane_off + acc * BN;
             if (p.epilogue == kSwiGLU) {
-                const int oc0 = (t % p.tiles_n) * (BN / 2);
+                const int oc0 = tile_n(p, t) * (BN / 2);
 #pragma unroll 1
                 for (int cc = 0; cc < BN / 64; ++cc) {
                     float g[32], u[32];

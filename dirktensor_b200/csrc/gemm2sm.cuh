@@ -156,9 +156,9 @@ gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
             int kit = 0;
             bool ok = true;
             for (int t = cluster; ok && t < p.num_tiles; t += nclusters) {
-                if (dt::gemm::tile_is_padding(p, (t / p.tiles_n) * kBM)) continue;
-                const int m0 = (t / p.tiles_n) * kBM + (int)rank * kHalf;
-                const int n0 = (t % p.tiles_n) * kBN + (int)rank * kHalf;
+                if (dt::gemm::tile_is_padding(p, dt::gemm::tile_m(p, t) * kBM)) continue;
+                const int m0 = dt::gemm::tile_m(p, t) * kBM + (int)rank * kHalf;
+                const int n0 = dt::gemm::tile_n(p, t) * kBN + (int)rank * kHalf;
                 for (int kb = 0; kb < nk; ++kb, ++kit) {
                     const int s = kit % kStages;
                     if (!mbar_wait(&sm.empty[s], ((kit / kStages) & 1) ^ 1, kSiteEmpty)) { ok = false; break; }
@@ -187,7 +187,7 @@ gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
             int kit = 0, it = 0;
             bool ok = true;
             for (int t = cluster; ok && t < p.num_tiles; t += nclusters) {
-                if (dt::gemm::tile_is_padding(p, (t / p.tiles_n) * kBM)) continue;
+                if (dt::gemm::tile_is_padding(p, dt::gemm::tile_m(p, t) * kBM)) continue;
                 const int acc = it & 1;
                 const uint32_t empty_phase = ((it >> 1) & 1) ^ 1;
                 ++it;
@@ -218,9 +218,9 @@ gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int it = 0;
         for (int t = cluster; t < p.num_tiles; t += nclusters) {
-            const int row = (t / p.tiles_n) * kBM + (int)rank * kHalf + q * 32 + lane;
-            const int n0 = (t % p.tiles_n) * kBN;
-            if (dt::gemm::tile_is_padding(p, (t / p.tiles_n) * kBM)) {
+            const int row = dt::gemm::tile_m(p, t) * kBM + (int)rank * kHalf + q * 32 + lane;
+            const int n0 = dt::gemm::tile_n(p, t) * kBN;
+            if (dt::gemm::tile_is_padding(p, dt::gemm::tile_m(p, t) * kBM)) {
                 if (p.pad_zero && p.epilogue == dt::gemm::kStore) {
                     float z[32];
 #pragma unroll
@@ -238,7 +238,7 @@ gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
             const uint32_t taddr = tmem + lane_off + acc * kBN;
             if (p.epilogue == dt::gemm::kSwiGLU) {
                 // Both CTAs hold all 256 columns of their rows: [0,128) gate, [128,256) up.
-                const int oc0 = (t % p.tiles_n) * (kBN / 2);
+                const int oc0 = dt::gemm::tile_n(p, t) * (kBN / 2);
 #pragma unroll 1
                 for (int cc = 0; cc < kBN / 64; ++cc) {
                     float g[32], u[32];
