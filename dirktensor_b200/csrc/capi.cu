@@ -1297,7 +1297,8 @@ int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void*
     const float* sm_l = reinterpret_cast<const float*>(rest + 4 * act + align256(M * H * 4));
     // scratch
     const size_t f32 = align256(M * d * 4), rows = flash_bwd_rows_bytes(B, T, H);
-    const size_t need = act + f32 + act + 2 * rows + 3 * f32 + align256(M * 3 * d * 2);
+    const long long nparts = (M + dt::elem::kBwdRows - 1) / dt::elem::kBwdRows;
+    const size_t need = act + f32 + act + 2 * rows + 3 * f32 + align256(M * 3 * d * 2) + align256(nparts * 2 * d * 4);
     if (a->bws_bytes < need) {
         if (a->bws) DT_CUDA(cudaFree(a->bws));
         a->bws = nullptr;
@@ -1315,6 +1316,7 @@ int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void*
     float* dk = dq + f32 / 4;
     float* dv = dk + f32 / 4;
     void* dqkv = w + 2 * act + 4 * f32 + 2 * rows;
+    float* gain_part = reinterpret_cast<float*>(w + 2 * act + 4 * f32 + 2 * rows + align256(M * 3 * d * 2));
     float* g_qkv = a->grad;
     float* g_o = a->grad + 3 * dd;
     float* g_qn = a->grad + 4 * dd;
@@ -1338,13 +1340,13 @@ int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void*
     np.sin_t = sin_t;
     np.cos_t = cos_t;
     np.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv);
-    np.dqg = g_qn;
-    np.dkg = g_kn;
+    np.gain_part = gain_part;
     np.M = M;
     np.T = T;
     np.eps = a->eps;
-    dt::elem::qk_norm_rope_bwd_kernel<<<(unsigned)((M + dt::elem::kBwdRows - 1) / dt::elem::kBwdRows),
-                                        dt::elem::kPrologueThreads, 0, st>>>(np);
+    dt::elem::qk_norm_rope_bwd_kernel<<<(unsigned)nparts, dt::elem::kPrologueThreads, 0, st>>>(np);
+    DT_CUDA(cudaGetLastError());
+    dt::elem::gain_grad_reduce_kernel<<<(2 * d + 255) / 256, 256, 0, st>>>(gain_part, (int)nparts, g_qn, g_kn);
     DT_CUDA(cudaGetLastError());
     DT_TRY(launch_gemm(dqkv, xb, g_qkv, 0, 3 * d, d, (int)M, d, st, 1, dt::gemm::kAccum, nullptr, 0, 0, 1,
                        1));  // d[Wq;Wk;Wv] += [dq|dk|dv]^T x

@@ -32,7 +32,12 @@ constexpr int kD = 128;
 constexpr int kBM = 128;  // rows of a Q or K/V block
 constexpr int kTileBytes = kBM * kD * 2;   // 32 KB: 128 rows x 128 dims bf16
 constexpr int kHalfBytes = kTileBytes / 2; // one 64-dim half (128-byte swizzle span)
-constexpr int kThreads = 192;              // warps 0-3 math (one thread per TMEM lane), 4 TMA, 5 MMA
+// warps 0-7 math: warp w owns TMEM lanes 32*(w%4)..+31 and column half w/4 of
+// every row (the backward's elementwise math needs no row reduction, so the two
+// halves never talk); warp 8 TMA, warp 9 MMA; warps 10-11 only complete the
+// third warpgroup (registers are granted per warpgroup).
+constexpr int kThreads = 384;
+constexpr int kTmaWarp = 8, kMmaWarp = 9;
 constexpr int kKvStages = 4;               // dq kernel: K_j, V_j ring (two key blocks in flight)
 
 // ---------------------------------------------------------------------------
@@ -135,6 +140,11 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int kk) {
     return umma_desc_sw128(tile + (uint32_t)(kk * 2048), kHalfBytes, 1024);
 }
 
+// TMEM column of the packed bf16 pairs for 16-wide step kk of a 128-column
+// S/dP tile: column half 0 packs into columns [0, 32), half 1 into [64, 96)
+// (each half overwrites only columns it has already read).
+__device__ __forceinline__ uint32_t packed_col(int kk) { return (uint32_t)(kk * 8 + (kk >= 4 ? 32 : 0)); }
+
 // ---------------------------------------------------------------------------
 // dK, dV: CTA = (b, h, key block kb); query blocks i = (causal ? kb : 0) .. nblk-1.
 // ---------------------------------------------------------------------------
@@ -178,16 +188,16 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             mbar_init(&sm.st_empty[s], 1);
         }
         mbar_init(&sm.s_full, 1);
-        mbar_init(&sm.pd_full, 4);
+        mbar_init(&sm.pd_full, 8);
         mbar_init(&sm.acc_done, 1);
         mbar_init(&sm.mma_done, 1);
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tmem_alloc(&sm.tmem_base, 512);
         tmem_relinquish();
     }
-    if (warp == 4 && lane == 0) {
+    if (warp == kTmaWarp && lane == 0) {
         tma_prefetch_desc(&tmap_q);
         tma_prefetch_desc(&tmap_k);
         tma_prefetch_desc(&tmap_v);
@@ -199,7 +209,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
     const uint32_t tmem = sm.tmem_base;
     const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
 
-    if (warp == 4) {
+    if (warp == kTmaWarp) {
         // ------------------------------ TMA producer ------------------------
         if (lane == 0) {
             mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
@@ -229,7 +239,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                     mbar_wait(&sm.st_full[it & 1], (it >> 1) & 1, kSiteLoad);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------ MMA issuer --------------------------
         if (lane == 0) {
             constexpr uint32_t idesc_ss = umma_idesc_bf16(kBM, kBM, 0, 0);  // both operands K-major
@@ -252,10 +262,10 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)  // dV += P^T dO   (16 queries per step)
-                    umma_ts(tdV, tS + kk * 8, desc_mnmajor(da, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(tdV, tS + packed_col(kk), desc_mnmajor(da, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)  // dK += dS^T Q
-                    umma_ts(tdK, tdP + kk * 8, desc_mnmajor(qa, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(tdK, tdP + packed_col(kk), desc_mnmajor(qa, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&sm.st_empty[s]);
             }
             if (ok) umma_commit(&sm.acc_done);
@@ -263,12 +273,14 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             mbar_wait(&sm.mma_done, 0, kSiteDone);
         }
         __syncwarp();
-    } else {
+    } else if (warp < 8) {
         // ------------------------------ math warps --------------------------
-        // thread = key row kr (TMEM lane); P^T / dS^T over 32-query chunks.
-        const int kr = warp * 32 + lane;
+        // thread = key row kr (TMEM lane); P^T / dS^T over the 64 queries of
+        // this warp's column half, in 32-query chunks.
+        const int hf = warp >> 2;
+        const int kr = (warp & 3) * 32 + lane;
         const int k_pos = kb * kBM + kr;
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const float c = p.scale_log2;
         bool ok = true;
         for (int it = 0; it < nq; ++it) {
@@ -278,7 +290,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             tc_fence_after();
             const bool diag = p.causal && (i == kb);
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int ch = 0; ch < 2; ++ch) {
+                const int cc = hf * 2 + ch;  // 32-query chunk of the 128
                 float sv[32], dp[32];
                 tmem_ld32(tS + lane_off + cc * 32, sv);
                 tmem_ld32(tdP + lane_off + cc * 32, dp);
@@ -302,10 +315,10 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                     pp[e] = pack_bf16x2(p0, p1);
                     pd[e] = pack_bf16x2(ds0, ds1);
                 }
-                // P^T / dS^T (bf16 pairs) over the first 64 columns of S^T / dP^T:
-                // chunk cc lands in columns [16cc, 16cc+16), already loaded.
-                tmem_st16(tS + lane_off + cc * 16, pp);
-                tmem_st16(tdP + lane_off + cc * 16, pd);
+                // P^T / dS^T as bf16 pairs: chunk ch of half hf lands in columns
+                // [64 hf + 16 ch, +16) of S^T / dP^T, which this warp has read.
+                tmem_st16(tS + lane_off + hf * 64 + ch * 16, pp);
+                tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -316,7 +329,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
         if (ok && nq > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc)) {
             tc_fence_after();
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = hf * 2; cc < hf * 2 + 2; ++cc) {
                 float a[32], bq[32];
                 tmem_ld32(tdK + lane_off + cc * 32, a);
                 tmem_ld32(tdV + lane_off + cc * 32, bq);
@@ -330,7 +343,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             float z[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) z[e] = 0.f;
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = hf * 2; cc < hf * 2 + 2; ++cc) {
                 store_row_chunk(p.dk, p, b, k_pos, h, cc * 32, z);
                 store_row_chunk(p.dv, p, b, k_pos, h, cc * 32, z);
             }
@@ -339,7 +352,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
@@ -384,16 +397,16 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
             mbar_init(&sm.kv_empty[s], 1);
         }
         mbar_init(&sm.s_full, 1);
-        mbar_init(&sm.ds_full, 4);
+        mbar_init(&sm.ds_full, 8);
         mbar_init(&sm.acc_done, 1);
         mbar_init(&sm.mma_done, 1);
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tmem_alloc(&sm.tmem_base, 512);
         tmem_relinquish();
     }
-    if (warp == 4 && lane == 0) {
+    if (warp == kTmaWarp && lane == 0) {
         tma_prefetch_desc(&tmap_q);
         tma_prefetch_desc(&tmap_k);
         tma_prefetch_desc(&tmap_v);
@@ -405,7 +418,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     const uint32_t tmem = sm.tmem_base;
     const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
 
-    if (warp == 4) {
+    if (warp == kTmaWarp) {
         // ------------------------------ TMA producer ------------------------
         if (lane == 0) {
             mbar_arrive_expect_tx(&sm.q_full, 2 * kTileBytes);
@@ -431,7 +444,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
                     mbar_wait(&sm.kv_full[L % kKvStages], (L / kKvStages) & 1, kSiteLoad);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------ MMA issuer --------------------------
         if (lane == 0) {
             constexpr uint32_t idesc_ss = umma_idesc_bf16(kBM, kBM, 0, 0);
@@ -473,7 +486,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
                 const uint32_t ka = smem_u32(sm.kv[stage(LK)]);
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)
-                    umma_ts(tdQ, tdP + kk * 8, desc_mnmajor(ka, kk), idesc_ts, (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(tdQ, tdP + packed_col(kk), desc_mnmajor(ka, kk), idesc_ts, (j > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&sm.kv_empty[stage(LK)]);
                 umma_commit(&sm.kv_empty[stage(LV)]);
                 // dP(j+1) after dQ(j) has read dS(j) from the same columns (in-order issue)
@@ -490,12 +503,14 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
             mbar_wait(&sm.mma_done, 0, kSiteDone);
         }
         __syncwarp();
-    } else {
+    } else if (warp < 8) {
         // ------------------------------ math warps --------------------------
-        // thread = query row r; dS over 32-key chunks, written over dP.
-        const int r = warp * 32 + lane;
+        // thread = query row r; dS over the 64 keys of this warp's column half
+        // in 32-key chunks, written over dP.
+        const int hf = warp >> 2;
+        const int r = (warp & 3) * 32 + lane;
         const int q_pos = qb * kBM + r;
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const long long srow = (long long)bh * p.Tpad + q_pos;  // q_pos < Tpad always
         const float lse_r = p.lse2[srow];
         const float d_r = p.dvec[srow];
@@ -507,7 +522,8 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
             const int k0 = j * kBM;
             const bool masked = (p.causal && j == qb) || (k0 + kBM > p.T);
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int ch = 0; ch < 2; ++ch) {
+                const int cc = hf * 2 + ch;  // 32-key chunk of the 128
                 float sv[32], dp[32];
                 tmem_ld32(tS + lane_off + cc * 32, sv);
                 tmem_ld32(tdP + lane_off + cc * 32, dp);
@@ -524,7 +540,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
                     }
                     pd[e] = pack_bf16x2(p0 * (dp[2 * e] - d_r) * p.scale, p1 * (dp[2 * e + 1] - d_r) * p.scale);
                 }
-                tmem_st16(tdP + lane_off + cc * 16, pd);
+                tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -534,7 +550,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         if (ok && nk > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc)) {
             tc_fence_after();
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = hf * 2; cc < hf * 2 + 2; ++cc) {
                 float a[32];
                 tmem_ld32(tdQ + lane_off + cc * 32, a);
                 tmem_wait_ld();
@@ -545,7 +561,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }

@@ -159,10 +159,12 @@ namespace elem {
 //   c = mean(dn * y),  dx = (g * dn - x_hat * c) / rms,  dg += dn * x_hat
 // (x = the projection before the norm, which the forward left in its fp32
 // [q|k|v] buffer).  Writes dx of q and k and the bf16 dV into one
-// [M, 3*2048] bf16 row (the operand of the projection-gradient GEMMs) and
-// adds the gain gradients into dqg / dkg.  A CTA of 256 threads walks
-// kBwdRows tokens with the forward's thread layout (thread = 4 RoPE pairs of
-// one head), keeping its gain-gradient partial sums in registers.
+// [M, 3*2048] bf16 row (the operand of the projection-gradient GEMMs).  A CTA
+// of 256 threads walks kBwdRows tokens with the forward's thread layout (thread
+// = 4 RoPE pairs of one head), keeping its gain-gradient partial sums in
+// registers and writing them to gain_part[blockIdx.x] (q gains, then k gains);
+// gain_grad_reduce_kernel then adds the partials in CTA order into dqg / dkg,
+// so the result does not depend on scheduling (no atomics).
 // ---------------------------------------------------------------------------
 constexpr int kBwdRows = 32;
 
@@ -178,8 +180,7 @@ struct NormRopeBwdParams {
     const float* sin_t;
     const float* cos_t;
     __nv_bfloat16* dqkv;  // [M, 3*2048]
-    float* dqg;           // [2048], accumulated
-    float* dkg;           // [2048], accumulated
+    float* gain_part;     // [gridDim.x, 2 * 2048] per-CTA partial gain gradients
     long long M;
     int T;
     float eps;
@@ -275,13 +276,23 @@ qk_norm_rope_bwd_kernel(const NormRopeBwdParams p) {
             make_uint4(pack_bf16x2(va.x, va.y), pack_bf16x2(va.z, va.w), pack_bf16x2(vb.x, vb.y),
                        pack_bf16x2(vb.z, vb.w));
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        atomicAdd(p.dqg + d_lo + e, accq[e]);
-        atomicAdd(p.dqg + d_hi + e, accq[4 + e]);
-        atomicAdd(p.dkg + d_lo + e, acck[e]);
-        atomicAdd(p.dkg + d_hi + e, acck[4 + e]);
-    }
+    float* part = p.gain_part + (long long)blockIdx.x * (2 * kDModel);
+    *reinterpret_cast<float4*>(part + d_lo) = make_float4(accq[0], accq[1], accq[2], accq[3]);
+    *reinterpret_cast<float4*>(part + d_hi) = make_float4(accq[4], accq[5], accq[6], accq[7]);
+    *reinterpret_cast<float4*>(part + kDModel + d_lo) = make_float4(acck[0], acck[1], acck[2], acck[3]);
+    *reinterpret_cast<float4*>(part + kDModel + d_hi) = make_float4(acck[4], acck[5], acck[6], acck[7]);
+}
+
+// Adds the per-CTA partial gain gradients [nparts, 2*2048] in order into
+// dqg [2048] and dkg [2048] (one thread per column).
+__global__ void gain_grad_reduce_kernel(const float* __restrict__ part, int nparts, float* __restrict__ dqg,
+                                        float* __restrict__ dkg) {
+    const int col = blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= 2 * kDModel) return;
+    float acc = 0.f;
+    for (int i = 0; i < nparts; ++i) acc += part[(long long)i * (2 * kDModel) + col];
+    if (col < kDModel) dqg[col] += acc;
+    else dkg[col - kDModel] += acc;
 }
 
 // SGD step (OlmoAttention.cpp:315-322, RMSNorm.cpp:38-41): w -= lr * g on the
