@@ -369,7 +369,8 @@ def main():
                          "ms_per_launch": ms_flash, "flops_per_launch": f_flash_rank, "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": 5 * args.steps,
+            # 3 casts + flash + O projection; the fused exchange adds its one-thread system fence
+            "gpu_launches": (6 if world > 1 and args.exchange == "fused" else 5) * args.steps,
             "clocks": clocks,
             "config1_t4096": t4096,
             "layers": layers,

@@ -843,8 +843,12 @@ int dt_flash_fwd_bf16_exchange(const void* q, const void* k, const void* v, void
     sc.plane = rank;
     sc.tokens_per_rank = tokens_per_rank;
     sc.dst = recv_bufs;
-    return launch_flash(q, k, v, nullptr, 1, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale,
-                        causal, reinterpret_cast<cudaStream_t>(stream), sc);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    DT_TRY(launch_flash(q, k, v, nullptr, 1, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale, causal,
+                        st, sc));
+    dt::elem::system_fence_kernel<<<1, 32, 0, st>>>();
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
 }
 
 typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);

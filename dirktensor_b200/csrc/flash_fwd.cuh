@@ -457,9 +457,6 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
             if (p.m_out) p.m_out[sidx] = m_o;
             if (p.l_out) p.l_out[sidx] = l_o;
         }
-        // rows stored into peers' memory become visible system-wide before the
-        // caller's stream-ordered barrier lets the owners read them
-        if (p.scatter_ranks > 0) __threadfence_system();
     }
 
     tc_fence_before();

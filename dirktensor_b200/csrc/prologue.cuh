@@ -30,6 +30,15 @@ __global__ void cast_f32_bf16_kernel(const float4* __restrict__ src, uint2* __re
     }
 }
 
+// One system-scope fence, launched on the stream right after a kernel that
+// stored into peers' memory: the stream orders that kernel's stores before
+// this fence, and the fence makes them visible system-wide before whatever
+// follows on the stream (the barrier after which the owners read them).  One
+// fence here replaces one per storing thread at the end of the kernel.
+__global__ void system_fence_kernel() {
+    if (threadIdx.x == 0) __threadfence_system();
+}
+
 // Three tensors in one launch (raw Q, K, V); blockIdx.y selects the tensor.
 struct Cast3 {
     const float4* src[3];

@@ -117,8 +117,10 @@ int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int 
  * straight into recv_bufs[g / tokens_per_rank] -- this GPU's own receive buffer
  * or a peer's, mapped with dt_ipc_open -- at plane `rank`, row
  * g % tokens_per_rank.  A receive buffer is [ranks][tokens_per_rank][H*D]
- * bf16, the planar A operand of dt_gemm_bf16_tn_planar.  The caller orders the
- * owners' reads after every rank's kernel (e.g. a one-element all-reduce on the
+ * bf16, the planar A operand of dt_gemm_bf16_tn_planar.  Two launches on
+ * `stream`: the attention kernel, then a one-thread system-scope fence that
+ * makes its peer stores visible system-wide.  The caller orders the owners'
+ * reads after every rank's launches (e.g. a one-element all-reduce on the
  * same stream) and double-buffers the receive buffers across steps. */
 int dt_flash_fwd_bf16_exchange(const void* q, const void* k, const void* v, void* const* recv_bufs, int ranks,
                                int rank, long long tokens_per_rank, float* softmax_m, float* softmax_l, int B, int T,
