@@ -38,7 +38,6 @@ constexpr int kHalfBytes = kTileBytes / 2; // one 64-dim half (128-byte swizzle 
 // third warpgroup (registers are granted per warpgroup).
 constexpr int kThreads = 384;
 constexpr int kTmaWarp = 8, kMmaWarp = 9;
-constexpr int kKvStages = 4;               // dq kernel: K_j, V_j ring (two key blocks in flight)
 
 // ---------------------------------------------------------------------------
 // Preprocessing: D[row] = O[row] . dO[row], lse2[row] = m*log2(e) + log2(l),
@@ -147,19 +146,33 @@ __device__ __forceinline__ uint32_t packed_col(int kk) { return (uint32_t)(kk * 
 
 // ---------------------------------------------------------------------------
 // dK, dV: CTA = (b, h, key block kb); query blocks i = (causal ? kb : 0) .. nblk-1.
+//
+// TMEM holds S^T, dP^T and the dV, dK accumulators (4 x 128 columns), so S^T and
+// dP^T have one buffer each; the math is split into two hand-offs so that it
+// overlaps the products anyway.  Issue order of the MMA thread, per query block i:
+//   [P_i ready]  dV += P_i^T dO_i,  S^T_{i+1} = K Q_{i+1}^T   (over P_i, in order)
+//   [dS_i ready] dK += dS_i^T Q_i,  dP^T_{i+1} = V dO_{i+1}^T (over dS_i, in order)
+// while the math warps compute P_i (from S^T_i), then dS_i (from dP^T_i and the P_i
+// they keep in registers), then P_{i+1} as soon as S^T_{i+1} lands.  Q_i (with its
+// lse2 and D rows) and dO_i sit in separate two-stage rings: dO_i is free after
+// dV_i, Q_i after dK_i.
 // ---------------------------------------------------------------------------
 struct __align__(1024) SmemKV {
     uint8_t k[kTileBytes];
     uint8_t v[kTileBytes];
     uint8_t q[2][kTileBytes];
     uint8_t dout[2][kTileBytes];
-    float lse[2][kBM];
-    float dvec[2][kBM];
+    float lse[2][kBM];   // travels with q[s]
+    float dvec[2][kBM];  // travels with q[s]: the dS phase reads it after dV_i may have freed dout[s]
     uint64_t kv_full;
-    uint64_t st_full[2];
-    uint64_t st_empty[2];
+    uint64_t q_full[2];
+    uint64_t q_empty[2];
+    uint64_t do_full[2];
+    uint64_t do_empty[2];
     uint64_t s_full;
-    uint64_t pd_full;
+    uint64_t dp_full;
+    uint64_t p_full;
+    uint64_t ds_full;
     uint64_t acc_done;
     uint64_t mma_done;
     uint32_t tmem_base;
@@ -184,11 +197,15 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
     if (threadIdx.x == 0) {
         mbar_init(&sm.kv_full, 1);
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&sm.st_full[s], 1);
-            mbar_init(&sm.st_empty[s], 1);
+            mbar_init(&sm.q_full[s], 1);
+            mbar_init(&sm.q_empty[s], 1);
+            mbar_init(&sm.do_full[s], 1);
+            mbar_init(&sm.do_empty[s], 1);
         }
         mbar_init(&sm.s_full, 1);
-        mbar_init(&sm.pd_full, 8);
+        mbar_init(&sm.dp_full, 1);
+        mbar_init(&sm.p_full, 8);
+        mbar_init(&sm.ds_full, 8);
         mbar_init(&sm.acc_done, 1);
         mbar_init(&sm.mma_done, 1);
         fence_mbar_init();
@@ -217,26 +234,32 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                 tma_load_4d(sm.k + hf * kHalfBytes, &tmap_k, &sm.kv_full, hf * 64, h, kb * kBM, b);
                 tma_load_4d(sm.v + hf * kHalfBytes, &tmap_v, &sm.kv_full, hf * 64, h, kb * kBM, b);
             }
-            int issued = 0;
+            int issued_q = 0, issued_do = 0;
             for (int it = 0; it < nq; ++it) {
                 const int s = it & 1;
-                if (!mbar_wait(&sm.st_empty[s], ((it >> 1) & 1) ^ 1, kSiteEmpty)) break;
+                const uint32_t empty_phase = ((it >> 1) & 1) ^ 1;
                 const int i = i0 + it;
-                mbar_arrive_expect_tx(&sm.st_full[s], 2 * kTileBytes + 2 * kBM * 4);
-                for (int hf = 0; hf < 2; ++hf) {
-                    tma_load_4d(sm.q[s] + hf * kHalfBytes, &tmap_q, &sm.st_full[s], hf * 64, h, i * kBM, b);
-                    tma_load_4d(sm.dout[s] + hf * kHalfBytes, &tmap_do, &sm.st_full[s], hf * 64, h, i * kBM, b);
-                }
+                if (!mbar_wait(&sm.q_empty[s], empty_phase, kSiteEmpty)) break;
+                mbar_arrive_expect_tx(&sm.q_full[s], kTileBytes + 2 * kBM * 4);
+                for (int hf = 0; hf < 2; ++hf)
+                    tma_load_4d(sm.q[s] + hf * kHalfBytes, &tmap_q, &sm.q_full[s], hf * 64, h, i * kBM, b);
                 const long long row0 = (long long)bh * p.Tpad + (long long)i * kBM;
-                bulk_load(sm.lse[s], p.lse2 + row0, kBM * 4, &sm.st_full[s]);
-                bulk_load(sm.dvec[s], p.dvec + row0, kBM * 4, &sm.st_full[s]);
-                ++issued;
+                bulk_load(sm.lse[s], p.lse2 + row0, kBM * 4, &sm.q_full[s]);
+                bulk_load(sm.dvec[s], p.dvec + row0, kBM * 4, &sm.q_full[s]);
+                ++issued_q;
+                if (!mbar_wait(&sm.do_empty[s], empty_phase, kSiteEmpty)) break;
+                mbar_arrive_expect_tx(&sm.do_full[s], kTileBytes);
+                for (int hf = 0; hf < 2; ++hf)
+                    tma_load_4d(sm.dout[s] + hf * kHalfBytes, &tmap_do, &sm.do_full[s], hf * 64, h, i * kBM, b);
+                ++issued_do;
             }
             if (error_raised()) {
                 // drain copies in flight before the CTA exits
                 mbar_wait(&sm.kv_full, 0, kSiteLoad);
-                for (int it = max(0, issued - 2); it < issued; ++it)
-                    mbar_wait(&sm.st_full[it & 1], (it >> 1) & 1, kSiteLoad);
+                for (int it = max(0, issued_q - 2); it < issued_q; ++it)
+                    mbar_wait(&sm.q_full[it & 1], (it >> 1) & 1, kSiteLoad);
+                for (int it = max(0, issued_do - 2); it < issued_do; ++it)
+                    mbar_wait(&sm.do_full[it & 1], (it >> 1) & 1, kSiteLoad);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -244,31 +267,65 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
         if (lane == 0) {
             constexpr uint32_t idesc_ss = umma_idesc_bf16(kBM, kBM, 0, 0);  // both operands K-major
             constexpr uint32_t idesc_ts = umma_idesc_bf16(kBM, kD, 0, 1);   // A in TMEM, B MN-major
-            bool ok = mbar_wait(&sm.kv_full, 0, kSiteLoad);
             const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
-            for (int it = 0; ok && it < nq; ++it) {
-                const int s = it & 1;
-                if (!mbar_wait(&sm.st_full[s], (it >> 1) & 1, kSiteLoad)) { ok = false; break; }
+            bool ok = mbar_wait(&sm.kv_full, 0, kSiteLoad);  // also drains the K/V copies when nq == 0
+            if (ok && nq > 0) ok = mbar_wait(&sm.q_full[0], 0, kSiteLoad);
+            if (ok && nq > 0) {
                 tc_fence_after();
-                const uint32_t qa = smem_u32(sm.q[s]), da = smem_u32(sm.dout[s]);
+                const uint32_t qa = smem_u32(sm.q[0]);
 #pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk)  // S^T = K Q^T  [keys x queries]
+                for (int kk = 0; kk < kD / 16; ++kk)  // S^T_0 = K Q_0^T  [keys x queries]
                     umma_ss(tS, desc_kmajor(ka, kk), desc_kmajor(qa, kk), idesc_ss, kk > 0 ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk)  // dP^T = V dO^T
-                    umma_ss(tdP, desc_kmajor(va, kk), desc_kmajor(da, kk), idesc_ss, kk > 0 ? 1u : 0u);
                 umma_commit(&sm.s_full);
-                if (!mbar_wait(&sm.pd_full, it & 1, kSiteP)) { ok = false; break; }
+                ok = mbar_wait(&sm.do_full[0], 0, kSiteLoad);
+            }
+            if (ok) {
+                tc_fence_after();
+                const uint32_t da = smem_u32(sm.dout[0]);
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk)  // dP^T_0 = V dO_0^T
+                    umma_ss(tdP, desc_kmajor(va, kk), desc_kmajor(da, kk), idesc_ss, kk > 0 ? 1u : 0u);
+                umma_commit(&sm.dp_full);
+            }
+            for (int it = 0; ok && it < nq; ++it) {
+                const int s = it & 1, s1 = s ^ 1;
+                const bool next = it + 1 < nq;
+                const uint32_t full_phase1 = ((it + 1) >> 1) & 1;
+                const uint32_t qa = smem_u32(sm.q[s]), da = smem_u32(sm.dout[s]);
+                if (!mbar_wait(&sm.p_full, it & 1, kSiteP)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)  // dV += P^T dO   (16 queries per step)
                     umma_ts(tdV, tS + packed_col(kk), desc_mnmajor(da, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&sm.do_empty[s]);
+                if (next) {
+                    // S^T_{i+1} over P_i: issued after dV, which reads P_i, in order
+                    if (!mbar_wait(&sm.q_full[s1], full_phase1, kSiteLoad)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t qa1 = smem_u32(sm.q[s1]);
+#pragma unroll
+                    for (int kk = 0; kk < kD / 16; ++kk)
+                        umma_ss(tS, desc_kmajor(ka, kk), desc_kmajor(qa1, kk), idesc_ss, kk > 0 ? 1u : 0u);
+                    umma_commit(&sm.s_full);
+                }
+                if (!mbar_wait(&sm.ds_full, it & 1, kSiteP)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)  // dK += dS^T Q
                     umma_ts(tdK, tdP + packed_col(kk), desc_mnmajor(qa, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&sm.st_empty[s]);
+                umma_commit(&sm.q_empty[s]);
+                if (next) {
+                    // dP^T_{i+1} over dS_i: issued after dK, which reads dS_i, in order
+                    if (!mbar_wait(&sm.do_full[s1], full_phase1, kSiteLoad)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t da1 = smem_u32(sm.dout[s1]);
+#pragma unroll
+                    for (int kk = 0; kk < kD / 16; ++kk)
+                        umma_ss(tdP, desc_kmajor(va, kk), desc_kmajor(da1, kk), idesc_ss, kk > 0 ? 1u : 0u);
+                    umma_commit(&sm.dp_full);
+                }
             }
-            if (ok) umma_commit(&sm.acc_done);
+            if (ok && nq > 0) umma_commit(&sm.acc_done);
             umma_commit(&sm.mma_done);
             mbar_wait(&sm.mma_done, 0, kSiteDone);
         }
@@ -276,7 +333,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
     } else if (warp < 8) {
         // ------------------------------ math warps --------------------------
         // thread = key row kr (TMEM lane); P^T / dS^T over the 64 queries of
-        // this warp's column half, in 32-query chunks.
+        // this warp's column half, in two 32-query chunks (unrolled, so that P
+        // stays in registers from the P phase to the dS phase).
         const int hf = warp >> 2;
         const int kr = (warp & 3) * 32 + lane;
         const int k_pos = kb * kBM + kr;
@@ -286,44 +344,61 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
         for (int it = 0; it < nq; ++it) {
             const int s = it & 1;
             const int i = i0 + it;
+            float pr[2][32];
             if (!mbar_wait(&sm.s_full, it & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
             const bool diag = p.causal && (i == kb);
-#pragma unroll 1
+#pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
                 const int cc = hf * 2 + ch;  // 32-query chunk of the 128
-                float sv[32], dp[32];
-                tmem_ld32(tS + lane_off + cc * 32, sv);
-                tmem_ld32(tdP + lane_off + cc * 32, dp);
+                tmem_ld32(tS + lane_off + cc * 32, pr[ch]);
                 tmem_wait_ld();
                 const float* lse = sm.lse[s] + cc * 32;
-                const float* dvec = sm.dvec[s] + cc * 32;
-                uint32_t pp[16], pd[16];
+                uint32_t pp[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const float2 l2 = *reinterpret_cast<const float2*>(lse + 2 * e);
-                    const float2 d2 = *reinterpret_cast<const float2*>(dvec + 2 * e);
-                    float p0 = ex2_approx(sv[2 * e] * c - l2.x);
-                    float p1 = ex2_approx(sv[2 * e + 1] * c - l2.y);
+                    float p0 = ex2_approx(pr[ch][2 * e] * c - l2.x);
+                    float p1 = ex2_approx(pr[ch][2 * e + 1] * c - l2.y);
                     if (diag) {
                         const int q = i * kBM + cc * 32 + 2 * e;
                         if (q < k_pos) p0 = 0.f;
                         if (q + 1 < k_pos) p1 = 0.f;
                     }
-                    const float ds0 = p0 * (dp[2 * e] - d2.x) * p.scale;
-                    const float ds1 = p1 * (dp[2 * e + 1] - d2.y) * p.scale;
+                    pr[ch][2 * e] = p0;
+                    pr[ch][2 * e + 1] = p1;
                     pp[e] = pack_bf16x2(p0, p1);
-                    pd[e] = pack_bf16x2(ds0, ds1);
                 }
-                // P^T / dS^T as bf16 pairs: chunk ch of half hf lands in columns
-                // [64 hf + 16 ch, +16) of S^T / dP^T, which this warp has read.
+                // P^T as bf16 pairs: chunk ch of half hf lands in columns
+                // [64 hf + 16 ch, +16) of S^T, which this warp has read.
                 tmem_st16(tS + lane_off + hf * 64 + ch * 16, pp);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.p_full);
+            if (!mbar_wait(&sm.dp_full, it & 1, kSiteS)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
+                const int cc = hf * 2 + ch;
+                float dp[32];
+                tmem_ld32(tdP + lane_off + cc * 32, dp);
+                tmem_wait_ld();
+                const float* dvec = sm.dvec[s] + cc * 32;
+                uint32_t pd[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float2 d2 = *reinterpret_cast<const float2*>(dvec + 2 * e);
+                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[2 * e] - d2.x) * p.scale,
+                                        pr[ch][2 * e + 1] * (dp[2 * e + 1] - d2.y) * p.scale);
+                }
                 tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.pd_full);
+            if (lane == 0) mbar_arrive(&sm.ds_full);
         }
         // ---- epilogue: dK, dV rows of this key block -------------------------
         if (ok && nq > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc)) {
@@ -360,20 +435,38 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
 
 // ---------------------------------------------------------------------------
 // dQ: CTA = (b, h, query block qb); key blocks j = 0 .. (causal ? qb : nblk-1).
+//
+// TMEM: S in two buffers (columns [0, 128) and [384, 512)), dP at [128, 256),
+// the dQ accumulator at [256, 384).  The MMA thread keeps S two key blocks
+// ahead: per block j, once dS_j is written back over dP_j it issues
+//   dQ += dS_j K_j,  dP_{j+1} = dO V_{j+1}^T (over dS_j, in order),
+//   S_{j+2} = Q K_{j+2}^T into the S buffer that S_j has left,
+// so the math warps compute P_{j+1} from S_{j+1} (already in TMEM) while dQ_j
+// and dP_{j+1} run, and only the dS phase waits for a product.  K blocks sit in
+// a three-stage ring (K_j serves S_j two blocks before dQ_j), V blocks in a
+// two-stage ring.
 // ---------------------------------------------------------------------------
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 struct __align__(1024) SmemQ {
     uint8_t q[kTileBytes];
     uint8_t dout[kTileBytes];
-    uint8_t kv[kKvStages][kTileBytes];  // K_0, V_0, K_1, V_1, ...
+    uint8_t k[kKStages][kTileBytes];
+    uint8_t v[kVStages][kTileBytes];
     uint64_t q_full;
-    uint64_t kv_full[kKvStages];
-    uint64_t kv_empty[kKvStages];
-    uint64_t s_full;
+    uint64_t k_full[kKStages];
+    uint64_t k_empty[kKStages];
+    uint64_t v_full[kVStages];
+    uint64_t v_empty[kVStages];
+    uint64_t s_full[2];
+    uint64_t dp_full;
     uint64_t ds_full;
     uint64_t acc_done;
     uint64_t mma_done;
     uint32_t tmem_base;
 };
+static_assert(sizeof(SmemQ) + 1024 <= 232448, "dq kernel shared memory exceeds 227 KB");
+static_assert(sizeof(SmemKV) + 1024 <= 232448, "dkdv kernel shared memory exceeds 227 KB");
 
 __global__ void __launch_bounds__(kThreads, 1)
 flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
@@ -392,11 +485,17 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
 
     if (threadIdx.x == 0) {
         mbar_init(&sm.q_full, 1);
-        for (int s = 0; s < kKvStages; ++s) {
-            mbar_init(&sm.kv_full[s], 1);
-            mbar_init(&sm.kv_empty[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&sm.k_full[s], 1);
+            mbar_init(&sm.k_empty[s], 1);
         }
-        mbar_init(&sm.s_full, 1);
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&sm.v_full[s], 1);
+            mbar_init(&sm.v_empty[s], 1);
+        }
+        mbar_init(&sm.s_full[0], 1);
+        mbar_init(&sm.s_full[1], 1);
+        mbar_init(&sm.dp_full, 1);
         mbar_init(&sm.ds_full, 8);
         mbar_init(&sm.acc_done, 1);
         mbar_init(&sm.mma_done, 1);
@@ -416,7 +515,8 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
-    const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
+    const uint32_t tdP = tmem + 128, tdQ = tmem + 256;
+    auto s_buf = [&](int j) { return (j & 1) ? tmem + 384 : tmem; };
 
     if (warp == kTmaWarp) {
         // ------------------------------ TMA producer ------------------------
@@ -426,22 +526,27 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
                 tma_load_4d(sm.q + hf * kHalfBytes, &tmap_q, &sm.q_full, hf * 64, h, qb * kBM, b);
                 tma_load_4d(sm.dout + hf * kHalfBytes, &tmap_do, &sm.q_full, hf * 64, h, qb * kBM, b);
             }
-            int issued = 0;
-            for (int L = 0; L < 2 * nk; ++L) {
-                const int s = L % kKvStages;
-                if (!mbar_wait(&sm.kv_empty[s], ((L / kKvStages) & 1) ^ 1, kSiteEmpty)) break;
-                mbar_arrive_expect_tx(&sm.kv_full[s], kTileBytes);
-                const int kt = (L >> 1) * kBM;
-                for (int hf = 0; hf < 2; ++hf) {
-                    if (L & 1) tma_load_4d(sm.kv[s] + hf * kHalfBytes, &tmap_v, &sm.kv_full[s], hf * 64, h, kt, b);
-                    else tma_load_4d(sm.kv[s] + hf * kHalfBytes, &tmap_k, &sm.kv_full[s], hf * 64, h, kt, b);
-                }
-                ++issued;
+            int issued_k = 0, issued_v = 0;
+            for (int j = 0; j < nk; ++j) {
+                const int sk = j % kKStages, sv = j % kVStages;
+                const int kt = j * kBM;
+                if (!mbar_wait(&sm.k_empty[sk], ((j / kKStages) & 1) ^ 1, kSiteEmpty)) break;
+                mbar_arrive_expect_tx(&sm.k_full[sk], kTileBytes);
+                for (int hf = 0; hf < 2; ++hf)
+                    tma_load_4d(sm.k[sk] + hf * kHalfBytes, &tmap_k, &sm.k_full[sk], hf * 64, h, kt, b);
+                ++issued_k;
+                if (!mbar_wait(&sm.v_empty[sv], ((j / kVStages) & 1) ^ 1, kSiteEmpty)) break;
+                mbar_arrive_expect_tx(&sm.v_full[sv], kTileBytes);
+                for (int hf = 0; hf < 2; ++hf)
+                    tma_load_4d(sm.v[sv] + hf * kHalfBytes, &tmap_v, &sm.v_full[sv], hf * 64, h, kt, b);
+                ++issued_v;
             }
             if (error_raised()) {
                 mbar_wait(&sm.q_full, 0, kSiteLoad);
-                for (int L = max(0, issued - kKvStages); L < issued; ++L)
-                    mbar_wait(&sm.kv_full[L % kKvStages], (L / kKvStages) & 1, kSiteLoad);
+                for (int j = max(0, issued_k - kKStages); j < issued_k; ++j)
+                    mbar_wait(&sm.k_full[j % kKStages], (j / kKStages) & 1, kSiteLoad);
+                for (int j = max(0, issued_v - kVStages); j < issued_v; ++j)
+                    mbar_wait(&sm.v_full[j % kVStages], (j / kVStages) & 1, kSiteLoad);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -449,64 +554,61 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         if (lane == 0) {
             constexpr uint32_t idesc_ss = umma_idesc_bf16(kBM, kBM, 0, 0);
             constexpr uint32_t idesc_ts = umma_idesc_bf16(kBM, kD, 0, 1);
-            auto stage = [](int L) { return L % kKvStages; };
-            auto phase = [](int L) { return (uint32_t)((L / kKvStages) & 1); };
             const uint32_t qa = smem_u32(sm.q), da = smem_u32(sm.dout);
-            bool ok = mbar_wait(&sm.q_full, 0, kSiteLoad);
-            if (ok) ok = mbar_wait(&sm.kv_full[stage(0)], phase(0), kSiteLoad);
-            if (ok) ok = mbar_wait(&sm.kv_full[stage(1)], phase(1), kSiteLoad);
-            if (ok) {
+            // S_j = Q K_j^T into buffer j & 1 (K_j must have landed)
+            auto issue_s = [&](int j) -> bool {
+                const int sk = j % kKStages;
+                if (!mbar_wait(&sm.k_full[sk], (j / kKStages) & 1, kSiteLoad)) return false;
                 tc_fence_after();
-                const uint32_t ka = smem_u32(sm.kv[stage(0)]), va = smem_u32(sm.kv[stage(1)]);
+                const uint32_t ka = smem_u32(sm.k[sk]);
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk)
-                    umma_ss(tS, desc_kmajor(qa, kk), desc_kmajor(ka, kk), idesc_ss, kk > 0 ? 1u : 0u);
+                    umma_ss(s_buf(j), desc_kmajor(qa, kk), desc_kmajor(ka, kk), idesc_ss, kk > 0 ? 1u : 0u);
+                umma_commit(&sm.s_full[j & 1]);
+                return true;
+            };
+            // dP_j = dO V_j^T (V_j must have landed; its stage is free once the product completes)
+            auto issue_dp = [&](int j) -> bool {
+                const int sv = j % kVStages;
+                if (!mbar_wait(&sm.v_full[sv], (j / kVStages) & 1, kSiteLoad)) return false;
+                tc_fence_after();
+                const uint32_t va = smem_u32(sm.v[sv]);
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk)
                     umma_ss(tdP, desc_kmajor(da, kk), desc_kmajor(va, kk), idesc_ss, kk > 0 ? 1u : 0u);
-                umma_commit(&sm.s_full);
-            }
+                umma_commit(&sm.dp_full);
+                umma_commit(&sm.v_empty[sv]);
+                return true;
+            };
+            bool ok = mbar_wait(&sm.q_full, 0, kSiteLoad);
+            if (ok && nk > 0) ok = issue_s(0);
+            if (ok && nk > 0) ok = issue_dp(0);
+            if (ok && nk > 1) ok = issue_s(1);
             for (int j = 0; ok && j < nk; ++j) {
-                const int LK = 2 * j, LV = 2 * j + 1, LK1 = 2 * j + 2, LV1 = 2 * j + 3;
-                const bool next = (j + 1) < nk;
                 if (!mbar_wait(&sm.ds_full, j & 1, kSiteP)) { ok = false; break; }
-                if (next) {
-                    if (!mbar_wait(&sm.kv_full[stage(LK1)], phase(LK1), kSiteLoad)) { ok = false; break; }
-                    if (!mbar_wait(&sm.kv_full[stage(LV1)], phase(LV1), kSiteLoad)) { ok = false; break; }
-                }
                 tc_fence_after();
-                // S(j+1) may overwrite S: the math warps have read S(j) (ds_full)
-                if (next) {
-                    const uint32_t ka1 = smem_u32(sm.kv[stage(LK1)]);
-#pragma unroll
-                    for (int kk = 0; kk < kD / 16; ++kk)
-                        umma_ss(tS, desc_kmajor(qa, kk), desc_kmajor(ka1, kk), idesc_ss, kk > 0 ? 1u : 0u);
-                }
-                // dQ += dS K_j  (dS: bf16 pairs over the first 64 columns of dP)
-                const uint32_t ka = smem_u32(sm.kv[stage(LK)]);
+                // dQ += dS_j K_j  (dS: bf16 pairs over the packed columns of dP)
+                const int sk = j % kKStages;
+                const uint32_t ka = smem_u32(sm.k[sk]);
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)
                     umma_ts(tdQ, tdP + packed_col(kk), desc_mnmajor(ka, kk), idesc_ts, (j > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&sm.kv_empty[stage(LK)]);
-                umma_commit(&sm.kv_empty[stage(LV)]);
-                // dP(j+1) after dQ(j) has read dS(j) from the same columns (in-order issue)
-                if (next) {
-                    const uint32_t va1 = smem_u32(sm.kv[stage(LV1)]);
-#pragma unroll
-                    for (int kk = 0; kk < kD / 16; ++kk)
-                        umma_ss(tdP, desc_kmajor(da, kk), desc_kmajor(va1, kk), idesc_ss, kk > 0 ? 1u : 0u);
-                    umma_commit(&sm.s_full);
-                }
+                umma_commit(&sm.k_empty[sk]);
+                // dP_{j+1} after dQ_j has read dS_j from the same columns (in-order issue)
+                if (j + 1 < nk && !issue_dp(j + 1)) { ok = false; break; }
+                // S_{j+2} into the buffer of S_j, which the math warps have read (ds_full)
+                if (j + 2 < nk && !issue_s(j + 2)) { ok = false; break; }
             }
-            if (ok) umma_commit(&sm.acc_done);
+            if (ok && nk > 0) umma_commit(&sm.acc_done);
             umma_commit(&sm.mma_done);
             mbar_wait(&sm.mma_done, 0, kSiteDone);
         }
         __syncwarp();
     } else if (warp < 8) {
         // ------------------------------ math warps --------------------------
-        // thread = query row r; dS over the 64 keys of this warp's column half
-        // in 32-key chunks, written over dP.
+        // thread = query row r; P then dS over the 64 keys of this warp's column
+        // half in two 32-key chunks (unrolled: P stays in registers), dS written
+        // over dP.
         const int hf = warp >> 2;
         const int r = (warp & 3) * 32 + lane;
         const int q_pos = qb * kBM + r;
@@ -517,29 +619,40 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         const float c = p.scale_log2;
         bool ok = true;
         for (int j = 0; j < nk; ++j) {
-            if (!mbar_wait(&sm.s_full, j & 1, kSiteS)) { ok = false; break; }
+            if (!mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
             const int k0 = j * kBM;
             const bool masked = (p.causal && j == qb) || (k0 + kBM > p.T);
-#pragma unroll 1
+            const uint32_t tS = s_buf(j);
+            float pr[2][32];
+#pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
                 const int cc = hf * 2 + ch;  // 32-key chunk of the 128
-                float sv[32], dp[32];
-                tmem_ld32(tS + lane_off + cc * 32, sv);
+                tmem_ld32(tS + lane_off + cc * 32, pr[ch]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    float pv = ex2_approx(pr[ch][e] * c - lse_r);
+                    if (masked) {
+                        const int key = k0 + cc * 32 + e;
+                        if ((p.causal && key > q_pos) || key >= p.T) pv = 0.f;
+                    }
+                    pr[ch][e] = pv;
+                }
+            }
+            if (!mbar_wait(&sm.dp_full, j & 1, kSiteS)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
+                const int cc = hf * 2 + ch;
+                float dp[32];
                 tmem_ld32(tdP + lane_off + cc * 32, dp);
                 tmem_wait_ld();
                 uint32_t pd[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    float p0 = ex2_approx(sv[2 * e] * c - lse_r);
-                    float p1 = ex2_approx(sv[2 * e + 1] * c - lse_r);
-                    if (masked) {
-                        const int key = k0 + cc * 32 + 2 * e;
-                        if ((p.causal && key > q_pos) || key >= p.T) p0 = 0.f;
-                        if ((p.causal && key + 1 > q_pos) || key + 1 >= p.T) p1 = 0.f;
-                    }
-                    pd[e] = pack_bf16x2(p0 * (dp[2 * e] - d_r) * p.scale, p1 * (dp[2 * e + 1] - d_r) * p.scale);
-                }
+                for (int e = 0; e < 16; ++e)
+                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[2 * e] - d_r) * p.scale,
+                                        pr[ch][2 * e + 1] * (dp[2 * e + 1] - d_r) * p.scale);
                 tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
             }
             tmem_wait_st();
