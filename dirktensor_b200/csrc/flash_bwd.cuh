@@ -348,27 +348,36 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             if (!mbar_wait(&sm.s_full, it & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
             const bool diag = p.causal && (i == kb);
+            // both 32-column loads in flight before the one wait
+            tmem_ld32(tS + lane_off + hf * 64, pr[0]);
+            tmem_ld32(tS + lane_off + hf * 64 + 32, pr[1]);
+            tmem_wait_ld();
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
-                const int cc = hf * 2 + ch;  // 32-query chunk of the 128
-                tmem_ld32(tS + lane_off + cc * 32, pr[ch]);
-                tmem_wait_ld();
-                const float* lse = sm.lse[s] + cc * 32;
+                const float* lse = sm.lse[s] + (hf * 2 + ch) * 32;
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float2 l2 = *reinterpret_cast<const float2*>(lse + e);
+                    pr[ch][e] = ex2_approx(pr[ch][e] * c - l2.x);
+                    pr[ch][e + 1] = ex2_approx(pr[ch][e + 1] * c - l2.y);
+                }
+            }
+            // The causal mask is a separate pass on the diagonal block only:
+            // written inside the loop above, its per-element tests cost more
+            // than the exponentials on every block.
+            if (diag) {
+                const int rel = k_pos - i * kBM - hf * 64;  // queries q < k_pos are masked
+#pragma unroll
+                for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (ch * 32 + e < rel) pr[ch][e] = 0.f;
+            }
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
                 uint32_t pp[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float2 l2 = *reinterpret_cast<const float2*>(lse + 2 * e);
-                    float p0 = ex2_approx(pr[ch][2 * e] * c - l2.x);
-                    float p1 = ex2_approx(pr[ch][2 * e + 1] * c - l2.y);
-                    if (diag) {
-                        const int q = i * kBM + cc * 32 + 2 * e;
-                        if (q < k_pos) p0 = 0.f;
-                        if (q + 1 < k_pos) p1 = 0.f;
-                    }
-                    pr[ch][2 * e] = p0;
-                    pr[ch][2 * e + 1] = p1;
-                    pp[e] = pack_bf16x2(p0, p1);
-                }
+                for (int e = 0; e < 16; ++e) pp[e] = pack_bf16x2(pr[ch][2 * e], pr[ch][2 * e + 1]);
                 // P^T as bf16 pairs: chunk ch of half hf lands in columns
                 // [64 hf + 16 ch, +16) of S^T, which this warp has read.
                 tmem_st16(tS + lane_off + hf * 64 + ch * 16, pp);
@@ -625,34 +634,38 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
             const bool masked = (p.causal && j == qb) || (k0 + kBM > p.T);
             const uint32_t tS = s_buf(j);
             float pr[2][32];
+            // both 32-column loads in flight before the one wait
+            tmem_ld32(tS + lane_off + hf * 64, pr[0]);
+            tmem_ld32(tS + lane_off + hf * 64 + 32, pr[1]);
+            tmem_wait_ld();
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch) {
-                const int cc = hf * 2 + ch;  // 32-key chunk of the 128
-                tmem_ld32(tS + lane_off + cc * 32, pr[ch]);
-                tmem_wait_ld();
+            for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float pv = ex2_approx(pr[ch][e] * c - lse_r);
-                    if (masked) {
-                        const int key = k0 + cc * 32 + e;
-                        if ((p.causal && key > q_pos) || key >= p.T) pv = 0.f;
-                    }
-                    pr[ch][e] = pv;
-                }
+                for (int e = 0; e < 32; ++e) pr[ch][e] = ex2_approx(pr[ch][e] * c - lse_r);
+            // Masks (the diagonal block, a partial last block) are a separate pass:
+            // written inside the loop above, their per-element tests cost more
+            // than the exponentials on every block.
+            if (masked) {
+                const int lim = (p.causal ? min(q_pos, p.T - 1) : p.T - 1) - (k0 + hf * 64);  // keys > lim are masked
+#pragma unroll
+                for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (ch * 32 + e > lim) pr[ch][e] = 0.f;
             }
             if (!mbar_wait(&sm.dp_full, j & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
+            float dp[2][32];
+            tmem_ld32(tdP + lane_off + hf * 64, dp[0]);
+            tmem_ld32(tdP + lane_off + hf * 64 + 32, dp[1]);
+            tmem_wait_ld();
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
-                const int cc = hf * 2 + ch;
-                float dp[32];
-                tmem_ld32(tdP + lane_off + cc * 32, dp);
-                tmem_wait_ld();
                 uint32_t pd[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
-                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[2 * e] - d_r) * p.scale,
-                                        pr[ch][2 * e + 1] * (dp[2 * e + 1] - d_r) * p.scale);
+                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[ch][2 * e] - d_r) * p.scale,
+                                        pr[ch][2 * e + 1] * (dp[ch][2 * e + 1] - d_r) * p.scale);
                 tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
             }
             tmem_wait_st();
