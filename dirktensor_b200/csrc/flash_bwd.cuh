@@ -148,14 +148,17 @@ __device__ __forceinline__ uint32_t packed_col(int kk) { return (uint32_t)(kk * 
 // dK, dV: CTA = (b, h, key block kb); query blocks i = (causal ? kb : 0) .. nblk-1.
 //
 // TMEM holds S^T, dP^T and the dV, dK accumulators (4 x 128 columns), so S^T and
-// dP^T have one buffer each; the math is split into two hand-offs so that it
-// overlaps the products anyway.  Issue order of the MMA thread, per query block i:
-//   [P_i ready]  dV += P_i^T dO_i,  S^T_{i+1} = K Q_{i+1}^T   (over P_i, in order)
-//   [dS_i ready] dK += dS_i^T Q_i,  dP^T_{i+1} = V dO_{i+1}^T (over dS_i, in order)
-// while the math warps compute P_i (from S^T_i), then dS_i (from dP^T_i and the P_i
-// they keep in registers), then P_{i+1} as soon as S^T_{i+1} lands.  Q_i (with its
-// lse2 and D rows) and dO_i sit in separate two-stage rings: dO_i is free after
-// dV_i, Q_i after dK_i.
+// dP^T have one buffer each.  The math warps load S^T_i, release its columns at
+// once (s_free) and keep P_i in registers; after dP^T_i lands they compute dS_i
+// and write P_i and dS_i, both as bf16 pairs, into the dP^T columns they have
+// read (per column half: dS into the first 32, P into the next 32).  So the MMA
+// thread issues S^T_{i+1} = K Q_{i+1}^T while P_i is still being computed, and
+// per query block:
+//   [S^T_i read]      S^T_{i+1}
+//   [P_i, dS_i ready] dV += P_i^T dO_i, dK += dS_i^T Q_i, dP^T_{i+1} = V dO_{i+1}^T
+//                     (the last over P_i / dS_i, in order).
+// Q_i (with its lse2 and D rows) and dO_i sit in separate two-stage rings: dO_i
+// is free after dV_i, Q_i after dK_i.
 // ---------------------------------------------------------------------------
 struct __align__(1024) SmemKV {
     uint8_t k[kTileBytes];
@@ -170,9 +173,9 @@ struct __align__(1024) SmemKV {
     uint64_t do_full[2];
     uint64_t do_empty[2];
     uint64_t s_full;
+    uint64_t s_free;
     uint64_t dp_full;
-    uint64_t p_full;
-    uint64_t ds_full;
+    uint64_t pds_full;
     uint64_t acc_done;
     uint64_t mma_done;
     uint32_t tmem_base;
@@ -203,9 +206,9 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             mbar_init(&sm.do_empty[s], 1);
         }
         mbar_init(&sm.s_full, 1);
+        mbar_init(&sm.s_free, 8);
         mbar_init(&sm.dp_full, 1);
-        mbar_init(&sm.p_full, 8);
-        mbar_init(&sm.ds_full, 8);
+        mbar_init(&sm.pds_full, 8);
         mbar_init(&sm.acc_done, 1);
         mbar_init(&sm.mma_done, 1);
         fence_mbar_init();
@@ -292,14 +295,9 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                 const bool next = it + 1 < nq;
                 const uint32_t full_phase1 = ((it + 1) >> 1) & 1;
                 const uint32_t qa = smem_u32(sm.q[s]), da = smem_u32(sm.dout[s]);
-                if (!mbar_wait(&sm.p_full, it & 1, kSiteP)) { ok = false; break; }
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < kBM / 16; ++kk)  // dV += P^T dO   (16 queries per step)
-                    umma_ts(tdV, tS + packed_col(kk), desc_mnmajor(da, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&sm.do_empty[s]);
                 if (next) {
-                    // S^T_{i+1} over P_i: issued after dV, which reads P_i, in order
+                    // S^T_{i+1} as soon as the math warps have read S^T_i
+                    if (!mbar_wait(&sm.s_free, it & 1, kSiteP)) { ok = false; break; }
                     if (!mbar_wait(&sm.q_full[s1], full_phase1, kSiteLoad)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t qa1 = smem_u32(sm.q[s1]);
@@ -308,14 +306,19 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                         umma_ss(tS, desc_kmajor(ka, kk), desc_kmajor(qa1, kk), idesc_ss, kk > 0 ? 1u : 0u);
                     umma_commit(&sm.s_full);
                 }
-                if (!mbar_wait(&sm.ds_full, it & 1, kSiteP)) { ok = false; break; }
+                if (!mbar_wait(&sm.pds_full, it & 1, kSiteP)) { ok = false; break; }
                 tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kBM / 16; ++kk)  // dV += P^T dO   (16 queries per step)
+                    umma_ts(tdV, tdP + 32 + packed_col(kk), desc_mnmajor(da, kk), idesc_ts,
+                            (it > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&sm.do_empty[s]);
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)  // dK += dS^T Q
                     umma_ts(tdK, tdP + packed_col(kk), desc_mnmajor(qa, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&sm.q_empty[s]);
                 if (next) {
-                    // dP^T_{i+1} over dS_i: issued after dK, which reads dS_i, in order
+                    // dP^T_{i+1} over P_i / dS_i: issued after dV and dK, which read them, in order
                     if (!mbar_wait(&sm.do_full[s1], full_phase1, kSiteLoad)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t da1 = smem_u32(sm.dout[s1]);
@@ -348,10 +351,14 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
             if (!mbar_wait(&sm.s_full, it & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
             const bool diag = p.causal && (i == kb);
-            // both 32-column loads in flight before the one wait
+            // both 32-column loads in flight before the one wait; then S^T's
+            // columns are free for the next block's product
             tmem_ld32(tS + lane_off + hf * 64, pr[0]);
             tmem_ld32(tS + lane_off + hf * 64 + 32, pr[1]);
             tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.s_free);
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
                 const float* lse = sm.lse[s] + (hf * 2 + ch) * 32;
@@ -373,41 +380,32 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                     for (int e = 0; e < 32; ++e)
                         if (ch * 32 + e < rel) pr[ch][e] = 0.f;
             }
-#pragma unroll
-            for (int ch = 0; ch < 2; ++ch) {
-                uint32_t pp[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) pp[e] = pack_bf16x2(pr[ch][2 * e], pr[ch][2 * e + 1]);
-                // P^T as bf16 pairs: chunk ch of half hf lands in columns
-                // [64 hf + 16 ch, +16) of S^T, which this warp has read.
-                tmem_st16(tS + lane_off + hf * 64 + ch * 16, pp);
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.p_full);
             if (!mbar_wait(&sm.dp_full, it & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
+            float dp[2][32];
+            tmem_ld32(tdP + lane_off + hf * 64, dp[0]);
+            tmem_ld32(tdP + lane_off + hf * 64 + 32, dp[1]);
+            tmem_wait_ld();
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
-                const int cc = hf * 2 + ch;
-                float dp[32];
-                tmem_ld32(tdP + lane_off + cc * 32, dp);
-                tmem_wait_ld();
-                const float* dvec = sm.dvec[s] + cc * 32;
-                uint32_t pd[16];
+                const float* dvec = sm.dvec[s] + (hf * 2 + ch) * 32;
+                uint32_t pd[16], pp[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const float2 d2 = *reinterpret_cast<const float2*>(dvec + 2 * e);
-                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[2 * e] - d2.x) * p.scale,
-                                        pr[ch][2 * e + 1] * (dp[2 * e + 1] - d2.y) * p.scale);
+                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[ch][2 * e] - d2.x) * p.scale,
+                                        pr[ch][2 * e + 1] * (dp[ch][2 * e + 1] - d2.y) * p.scale);
+                    pp[e] = pack_bf16x2(pr[ch][2 * e], pr[ch][2 * e + 1]);
                 }
+                // chunk ch of half hf: dS^T into columns [64 hf + 16 ch, +16) and
+                // P^T into [64 hf + 32 + 16 ch, +16) of dP^T, all read above
                 tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
+                tmem_st16(tdP + lane_off + hf * 64 + 32 + ch * 16, pp);
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.ds_full);
+            if (lane == 0) mbar_arrive(&sm.pds_full);
         }
         // ---- epilogue: dK, dV rows of this key block -------------------------
         if (ok && nq > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc)) {
