@@ -308,15 +308,17 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_c
                 }
                 if (!mbar_wait(&sm.pds_full, it & 1, kSiteP)) { ok = false; break; }
                 tc_fence_after();
+                // dK first: its completion frees the Q stage that Q_{i+2} loads into,
+                // and that load is on the way to S^T_{i+2}
+#pragma unroll
+                for (int kk = 0; kk < kBM / 16; ++kk)  // dK += dS^T Q
+                    umma_ts(tdK, tdP + packed_col(kk), desc_mnmajor(qa, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&sm.q_empty[s]);
 #pragma unroll
                 for (int kk = 0; kk < kBM / 16; ++kk)  // dV += P^T dO   (16 queries per step)
                     umma_ts(tdV, tdP + 32 + packed_col(kk), desc_mnmajor(da, kk), idesc_ts,
                             (it > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&sm.do_empty[s]);
-#pragma unroll
-                for (int kk = 0; kk < kBM / 16; ++kk)  // dK += dS^T Q
-                    umma_ts(tdK, tdP + packed_col(kk), desc_mnmajor(qa, kk), idesc_ts, (it > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&sm.q_empty[s]);
                 if (next) {
                     // dP^T_{i+1} over P_i / dS_i: issued after dV and dK, which read them, in order
                     if (!mbar_wait(&sm.do_full[s1], full_phase1, kSiteLoad)) { ok = false; break; }
