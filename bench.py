@@ -5,10 +5,12 @@ Workload (every N): configuration 4 -- head-parallel long-context attention,
 B=16, T=6144, H=16, D=128, Q/K/V fp32 N(0,1) (seeded synthetic data), causal,
 scale 1/sqrt(128), followed by the O projection (Wo 2048x2048, N(0, 0.02)).
 With N GPUs rank r owns heads [r*16/N, (r+1)*16/N); per-head outputs are
-exchanged token-sliced (NCCL all-to-all) and each rank projects B*T/N tokens.
+exchanged token-sliced (by the attention kernel's own NVLink stores, or an NCCL
+all-to-all with --exchange nccl) and each rank projects B*T/N tokens.
 Total work is fixed, so scaling is "strong".
 
-A step = cast Q/K/V to bf16 -> flash attention -> exchange -> O projection.
+A step = cast K/V to bf16 -> flash attention (reads the fp32 Q rows and rounds them
+itself) -> exchange -> O projection.
 value      = (attention FLOPs 2*B*H*T^2*D + O-proj FLOPs 2*B*T*d^2) / step time,
              device-resident inputs, CUDA events on the launching stream, max over ranks.
 e2e        = the same through host buffers: pinned Q/K/V slices copied in and the
@@ -369,8 +371,9 @@ def main():
                          "ms_per_launch": ms_flash, "flops_per_launch": f_flash_rank, "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            # 3 casts + flash + O projection; the fused exchange adds its one-thread system fence
-            "gpu_launches": (6 if world > 1 and args.exchange == "fused" else 5) * args.steps,
+            # K and V casts + flash (which rounds fp32 Q itself) + O projection; the fused exchange
+            # adds its one-thread system fence
+            "gpu_launches": (5 if world > 1 and args.exchange == "fused" else 4) * args.steps,
             "clocks": clocks,
             "config1_t4096": t4096,
             "layers": layers,

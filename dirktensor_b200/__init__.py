@@ -15,6 +15,7 @@ from .attention import (  # noqa: F401
     flash_attention_backward,
     flash_attention_forward,
     flash_attention_forward_bf16,
+    flash_attention_forward_qf32,
     gemm_bf16,
     gemm_bf16_tn,
     head_dim,

@@ -94,10 +94,13 @@ SIGNATURES = {
     "dt_flash_fwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "dt_flash_fwd_bf16_exchange": (_I, [_P, _P, _P, ctypes.POINTER(_P), _I, _I, _LL, _P, _P, _I, _I, _I, _I, _F, _I,
                                         _P]),
+    "dt_flash_fwd_qf32_exchange": (_I, [_P, _P, _P, ctypes.POINTER(_P), _I, _I, _LL, _P, _P, _I, _I, _I, _I, _F, _I,
+                                        _P]),
     "dt_ipc_get_handle": (_I, [_P, _P, ctypes.POINTER(_SZ)]),
     "dt_ipc_open": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
     "dt_ipc_close": (_I, [_P, _SZ]),
     "dt_flash_fwd_bf16": (_I, [_P, _P, _P, _P, _I, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
+    "dt_flash_fwd_qf32": (_I, [_P, _P, _P, _P, _I, _LL, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "dt_attn_create": (_I, [ctypes.POINTER(dt_attn_weights), _I, ctypes.POINTER(_P)]),
     "dt_attn_create_from_npy": (_I, [ctypes.c_char_p, ctypes.c_uint, _I, ctypes.POINTER(_P)]),
     "dt_attn_forward": (_I, [_P, _P, _I, _I, _P, _P, _P]),

@@ -177,6 +177,29 @@ def flash_attention_forward_bf16(q, k, v, scale: float, causal: bool = True, out
     return out
 
 
+def flash_attention_forward_qf32(q, k, v, scale: float, causal: bool = True, out=None, out_bf16: bool = False,
+                                 out_row_stride: Optional[int] = None, softmax_m=None, softmax_l=None,
+                                 seq_lens=None):
+    """q float32, k and v bf16 CUDA tensors [B, T, H, D]: the attention kernel
+    rounds the rows of q to bf16 itself (no separate cast pass over q)."""
+    torch = _torch()
+    if not (q.is_cuda and q.dtype == torch.float32 and q.is_contiguous() and q.dim() == 4):
+        raise ValueError("q must be a contiguous float32 CUDA tensor [B, T, H, D]")
+    for n, t in (("k", k), ("v", v)):
+        if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.shape == q.shape):
+            raise ValueError(f"{n} must be a contiguous bfloat16 CUDA tensor shaped like q")
+    B, T, H, D = q.shape
+    if out is None:
+        out = torch.empty((B, T, H, D), dtype=torch.bfloat16 if out_bf16 else torch.float32, device=q.device)
+        out_row_stride = H * D
+    if out_row_stride is None:
+        out_row_stride = H * D
+    check(lib().dt_flash_fwd_qf32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), int(out_bf16),
+                                  int(out_row_stride), _ptr(softmax_m), _ptr(softmax_l), _ptr(seq_lens), B, T, H,
+                                  D, float(scale), int(bool(causal)), _stream_ptr(q.device)))
+    return out
+
+
 def cast_bf16(x):
     """bf16 copy of a float32 CUDA tensor (element count a multiple of 4)."""
     torch = _torch()

@@ -277,8 +277,9 @@ int launch_cast(const float* src, void* dst, long long n, cudaStream_t st) {
     return DT_OK;
 }
 
+// Casts the first `count` (1..3) of a, b, c in one launch.
 int launch_cast3(const float* a, const float* b, const float* c, void* da, void* db, void* dc, long long n,
-                 cudaStream_t st) {
+                 cudaStream_t st, int count = 3) {
     if (n == 0) return DT_OK;
     dt::elem::Cast3 args;
     args.src[0] = reinterpret_cast<const float4*>(a);
@@ -291,7 +292,7 @@ int launch_cast3(const float* a, const float* b, const float* c, void* da, void*
     const int threads = 256;
     long long blocks = (n4 + threads - 1) / threads;
     if (blocks > 148 * 8) blocks = 148 * 8;
-    dt::elem::cast3_f32_bf16_kernel<<<dim3((unsigned)blocks, 3), threads, 0, st>>>(args, n4);
+    dt::elem::cast3_f32_bf16_kernel<<<dim3((unsigned)blocks, (unsigned)count), threads, 0, st>>>(args, n4);
     DT_CUDA(cudaGetLastError());
     return DT_OK;
 }
@@ -303,12 +304,14 @@ struct Scatter {
     void* const* dst = nullptr;
 };
 
+// q: bf16 [B, T, H, D] read through a tensor map, or, when q_f32 is given, unused
+// (the kernel reads the fp32 rows itself; the K map stands in for the Q map).
 int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
                  float* m, float* l, const int* seq_lens, int B, int T, int H, float scale, int causal,
-                 cudaStream_t st, const Scatter& sc = Scatter()) {
+                 cudaStream_t st, const Scatter& sc = Scatter(), const float* q_f32 = nullptr) {
     if ((long long)B * T * H == 0) return DT_OK;
     CUtensorMap mq, mk, mv;
-    DT_TRY(make_map_bthd(&mq, q, B, T, H, 128));
+    DT_TRY(make_map_bthd(&mq, q_f32 ? k : q, B, T, H, 128));
     DT_TRY(make_map_bthd(&mk, k, B, T, H, 128));
     DT_TRY(make_map_bthd(&mv, v, B, T, H, 128));
     dt::flash::Params p{};
@@ -348,6 +351,8 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     p.scatter_plane = sc.plane;
     p.tokens_per_rank = sc.tokens_per_rank;
     for (int r = 0; r < 8; ++r) p.scatter_dst[r] = (r < sc.ranks) ? sc.dst[r] : nullptr;
+    p.q_f32 = q_f32;
+    p.q_row_stride = (long long)H * 128;
     const long long grid = (long long)p.nblk * B * H;
     if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
     dt::flash::flash_fwd_kernel<<<(unsigned)grid, dt::flash::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
@@ -614,9 +619,10 @@ int dt_flash_fwd(const float* q, const float* k, const float* v, float* o, float
     const long long n = (long long)B * T * H * D;
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
     const size_t one = align256((size_t)n * 2);
-    DT_TRY(launch_cast3(q, k, v, ws, ws + one, ws + 2 * one, n, st));
-    return launch_flash(ws, ws + one, ws + 2 * one, o, 0, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H,
-                        scale, causal, st);
+    // K and V to bf16; the attention kernel reads the fp32 Q rows itself
+    DT_TRY(launch_cast3(k, v, nullptr, ws + one, ws + 2 * one, nullptr, n, st, 2));
+    return launch_flash(nullptr, ws + one, ws + 2 * one, o, 0, (long long)H * D, softmax_m, softmax_l, nullptr, B, T,
+                        H, scale, causal, st, Scatter(), q);
 }
 
 int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, float* softmax_m,
@@ -649,9 +655,9 @@ int dt_flash_fwd_host(const float* q, const float* k, const float* v, float* o, 
     const long long nn = (long long)n;
     uint8_t* w = reinterpret_cast<uint8_t*>(dws);
     const size_t one = align256(n * 2);
-    DT_TRY(launch_cast3(dq, dk, dv, w, w + one, w + 2 * one, nn, st));
-    DT_TRY(launch_flash(w, w + one, w + 2 * one, dout, 0, (long long)H * D, dm, dl, nullptr, B, T, H, scale, causal,
-                        st));
+    DT_TRY(launch_cast3(dk, dv, nullptr, w + one, w + 2 * one, nullptr, nn, st, 2));
+    DT_TRY(launch_flash(nullptr, w + one, w + 2 * one, dout, 0, (long long)H * D, dm, dl, nullptr, B, T, H, scale,
+                        causal, st, Scatter(), dq));
     DT_CUDA(cudaMemcpyAsync(o, dout, n * 4, cudaMemcpyDeviceToHost, st));
     if (softmax_m) DT_CUDA(cudaMemcpyAsync(softmax_m, dm, ns * 4, cudaMemcpyDeviceToHost, st));
     if (softmax_l) DT_CUDA(cudaMemcpyAsync(softmax_l, dl, ns * 4, cudaMemcpyDeviceToHost, st));
@@ -846,6 +852,53 @@ int dt_flash_fwd_bf16_exchange(const void* q, const void* k, const void* v, void
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     DT_TRY(launch_flash(q, k, v, nullptr, 1, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale, causal,
                         st, sc));
+    dt::elem::system_fence_kernel<<<1, 32, 0, st>>>();
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int dt_flash_fwd_qf32(const float* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
+                      float* softmax_m, float* softmax_l, const int* seq_lens, int B, int T, int H, int D,
+                      float scale, int causal, void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (!q || !k || !v || !o) return fail(DT_ERR_INVALID_ARGUMENT, "null q/k/v/o");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v/o must be 16-byte aligned");
+    if (o_row_stride < (long long)H * D || (o_row_stride % 8) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "o_row_stride must be >= H*D and a multiple of 8");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    return launch_flash(nullptr, k, v, o, o_bf16 ? 1 : 0, o_row_stride, softmax_m, softmax_l, seq_lens, B, T, H,
+                        scale, causal, reinterpret_cast<cudaStream_t>(stream), Scatter(), q);
+}
+
+int dt_flash_fwd_qf32_exchange(const float* q, const void* k, const void* v, void* const* recv_bufs, int ranks,
+                               int rank, long long tokens_per_rank, float* softmax_m, float* softmax_l, int B, int T,
+                               int H, int D, float scale, int causal, void* stream) {
+    t_last_error.clear();
+    DT_TRY(check_flash_shape(B, T, H, D));
+    if ((long long)B * T * H == 0) return DT_OK;
+    if (ranks < 1 || ranks > 8 || rank < 0 || rank >= ranks)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ranks must be 1..8 and 0 <= rank < ranks");
+    if (!recv_bufs || tokens_per_rank <= 0 || tokens_per_rank * ranks != (long long)B * T)
+        return fail(DT_ERR_INVALID_ARGUMENT, "tokens_per_rank * ranks must equal B*T");
+    if (!q || !k || !v || !aligned16(q) || !aligned16(k) || !aligned16(v))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v must be non-null and 16-byte aligned");
+    for (int r = 0; r < ranks; ++r)
+        if (!recv_bufs[r] || !aligned16(recv_bufs[r]))
+            return fail(DT_ERR_INVALID_ARGUMENT, "receive buffer %d must be non-null and 16-byte aligned", r);
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    Scatter sc;
+    sc.ranks = ranks;
+    sc.plane = rank;
+    sc.tokens_per_rank = tokens_per_rank;
+    sc.dst = recv_bufs;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    DT_TRY(launch_flash(nullptr, k, v, nullptr, 1, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale,
+                        causal, st, sc, q));
     dt::elem::system_fence_kernel<<<1, 32, 0, st>>>();
     DT_CUDA(cudaGetLastError());
     return DT_OK;

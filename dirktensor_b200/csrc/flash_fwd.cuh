@@ -75,6 +75,12 @@ struct Params {
     int scatter_plane;
     long long tokens_per_rank;
     void* scatter_dst[8];
+    // fp32 Q (null: Q arrives as bf16 through tmap_q).  The softmax warps read
+    // their own rows ([B, T, H, D], q_row_stride elements between tokens), round
+    // them to bf16 and write the swizzled tile the tensor map would have written,
+    // which removes the separate fp32 -> bf16 pass over Q.
+    const float* q_f32;
+    long long q_row_stride;
 };
 
 struct __align__(1024) Smem {
@@ -159,7 +165,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     const int nkv = max(n_t0, n_t1);
 
     if (threadIdx.x == 0) {
-        mbar_init(&sm.q_full, 1);
+        mbar_init(&sm.q_full, p.q_f32 ? 8 : 1);  // 8 softmax warps, or the TMA transaction
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.kv_full[s], 1);
             mbar_init(&sm.kv_empty[s], 1);
@@ -189,10 +195,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     if (warp == 8) {
         // ------------------------------ TMA producer ------------------------
         if (lane == 0 && nkv > 0) {
-            mbar_arrive_expect_tx(&sm.q_full, kQTiles * kTileBytes);
-            for (int i = 0; i < kQTiles; ++i)
-                for (int hf = 0; hf < 2; ++hf)
-                    tma_load_4d(sm.q[i] + hf * kHalfBytes, &tmap_q, &sm.q_full, hf * 64, h, q0 + i * kBM, b);
+            if (!p.q_f32) {
+                mbar_arrive_expect_tx(&sm.q_full, kQTiles * kTileBytes);
+                for (int i = 0; i < kQTiles; ++i)
+                    for (int hf = 0; hf < 2; ++hf)
+                        tma_load_4d(sm.q[i] + hf * kHalfBytes, &tmap_q, &sm.q_full, hf * 64, h, q0 + i * kBM, b);
+            }
             int issued = 0;
             for (int L = 0; L < 2 * nkv; ++L) {
                 const int s = L % kStages;
@@ -277,6 +285,35 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         __syncwarp();
     } else if (warp < 8) {
         // --------------------------- softmax warpgroups ---------------------
+        if (p.q_f32) {
+            // This warp's 32 rows of Q tile (warp >> 2), fp32 -> bf16, in the
+            // 128-byte-swizzled K-major layout of a TMA load: row r of a 64-dim
+            // half at r * 128, its 16-byte chunk c at position c ^ (r & 7).  One
+            // coalesced 512-byte row per load instruction (lane = 4 dims), all 32
+            // rows' loads in flight at once (with 8 in flight the four
+            // round trips to DRAM per CTA cost more than the cast they replace);
+            // rows at or past T are zeros, as the tensor map fills them.
+            const uint32_t qs = smem_u32(sm.q[warp >> 2]);
+            const int chunk = lane >> 1;  // 16-byte chunk (8 dims) of this lane's 4 dims
+            const uint32_t col = (uint32_t)(chunk >> 3) * kHalfBytes + (uint32_t)(lane & 1) * 8;
+#pragma unroll 32
+            for (int rr = 0; rr < 32; ++rr) {
+                const int row = (warp & 3) * 32 + rr;
+                const int t = q0 + (warp >> 2) * kBM + row;
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t < p.T)
+                    x = __ldg(reinterpret_cast<const float4*>(p.q_f32 + ((long long)b * p.T + t) * p.q_row_stride +
+                                                              (long long)h * kD) + lane);
+                const uint32_t addr = qs + col + (uint32_t)row * 128 + ((uint32_t)((chunk & 7) ^ (row & 7)) << 4);
+                asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(pack_bf16x2(x.x, x.y)),
+                             "r"(pack_bf16x2(x.z, x.w))
+                             : "memory");
+            }
+            // generic-proxy stores become visible to the tensor cores' reads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.q_full);
+        }
         const int i = warp >> 2;          // Q tile
         const int r = (warp & 3) * 32 + lane;
         const int qt = q0 + i * kBM;

@@ -97,11 +97,11 @@ class HeadParallelAttention:
     def local_attention(self, q, k, v, scale: float, causal: bool, events=None) -> torch.Tensor:
         """Flash attention on this rank's heads -> bf16 [M, Hl*D]."""
         B, T, Hl, D = q.shape
-        qb, kb, vb = (_attn.cast_bf16(t) for t in (q, k, v))
+        kb, vb = (_attn.cast_bf16(t) for t in (k, v))  # the attention kernel rounds q itself
         out = self._buf("o_local", (B * T, Hl * D), torch.bfloat16, q.device)
         if events is not None:
             events[0].record()
-        _attn.flash_attention_forward_bf16(qb, kb, vb, scale, causal, out=out, out_bf16=True,
+        _attn.flash_attention_forward_qf32(q.contiguous(), kb, vb, scale, causal, out=out, out_bf16=True,
                                            out_row_stride=Hl * D)
         if events is not None:
             events[1].record()
@@ -186,10 +186,11 @@ class HeadParallelAttention:
         self._setup_fused(M, Hl * D, q.device)
         buf = self._step & 1
         self._step += 1
-        qb, kb, vb = (_attn.cast_bf16(t) for t in (q, k, v))
+        kb, vb = (_attn.cast_bf16(t) for t in (k, v))  # the attention kernel rounds q itself
+        q = q.contiguous()
         if events is not None:
             events[0].record()
-        check(lib().dt_flash_fwd_bf16_exchange(qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), self._fused[2][buf],
+        check(lib().dt_flash_fwd_qf32_exchange(q.data_ptr(), kb.data_ptr(), vb.data_ptr(), self._fused[2][buf],
                                                self.world, self.rank, M // self.world, None, None, B, T, Hl, D,
                                                float(scale), int(bool(causal)),
                                                torch.cuda.current_stream(q.device).cuda_stream))

@@ -63,7 +63,9 @@ int dt_selftest_expired_wait(void);
  * softmax_m = row max of the scaled scores, softmax_l = sum exp(s - m).
  * q, k, v, o: [B, T, H, D] fp32 device pointers; softmax_m/l may be NULL.
  * D must be 128.  Operands are rounded to bf16 for the tensor cores
- * (fp32 accumulation and softmax); the workspace holds those bf16 copies. */
+ * (fp32 accumulation and softmax); the workspace holds the bf16 copies of K
+ * and V (its first third, sized for Q, is unused: the attention kernel rounds
+ * the rows of Q itself). */
 size_t dt_flash_fwd_workspace_bytes(int B, int T, int H, int D);
 int dt_flash_fwd(const float* q, const float* k, const float* v, float* o, float* softmax_m, float* softmax_l,
                  int B, int T, int H, int D, float scale, int causal, void* workspace, size_t workspace_bytes,
@@ -123,6 +125,17 @@ int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int 
  * reads after every rank's launches (e.g. a one-element all-reduce on the
  * same stream) and double-buffers the receive buffers across steps. */
 int dt_flash_fwd_bf16_exchange(const void* q, const void* k, const void* v, void* const* recv_bufs, int ranks,
+                               int rank, long long tokens_per_rank, float* softmax_m, float* softmax_l, int B, int T,
+                               int H, int D, float scale, int causal, void* stream);
+
+/* Same as dt_flash_fwd_bf16 and dt_flash_fwd_bf16_exchange, with Q given as fp32
+ * [B, T, H, D] (K and V bf16): the attention kernel reads the fp32 rows of Q
+ * and rounds them to bf16 itself, so no separate cast pass over Q is needed.
+ * Results are identical to casting Q with dt_cast_f32_bf16 first. */
+int dt_flash_fwd_qf32(const float* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
+                      float* softmax_m, float* softmax_l, const int* seq_lens, int B, int T, int H, int D,
+                      float scale, int causal, void* stream);
+int dt_flash_fwd_qf32_exchange(const float* q, const void* k, const void* v, void* const* recv_bufs, int ranks,
                                int rank, long long tokens_per_rank, float* softmax_m, float* softmax_l, int B, int T,
                                int H, int D, float scale, int causal, void* stream);
 /* CUDA IPC for the exchange buffers.  dt_ipc_get_handle writes the 64-byte
