@@ -25,8 +25,9 @@ Two exchange modes:
       shared memory so that each warp stores two whole 256-byte rows per
       instruction to the peer; one system-scope fence kernel after the
       attention kernel (not one fence per storing thread) publishes the stores.
-      Measured at 2 GPUs (config 4): 1.75 ms per step against 2.09 ms for the
-      NCCL path.
+      The attention kernel reads this rank's Q in fp32 and rounds it itself
+      (K and V are cast first).  Measured at 2 GPUs (config 4): 1.70 ms per
+      step; 2.09 ms for the NCCL path.
   nccl: the flash kernel writes a local [M, Hl*D] buffer and
       torch.distributed.all_to_all_single moves the token slices.
 The attention and projection kernels are the CUDA library's.
