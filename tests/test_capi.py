@@ -59,6 +59,43 @@ def test_argument_validation_without_device():
     assert st == 6 and b"cannot open" in L.dt_last_error()
 
 
+def test_qf32_entry_points_validate_before_device():
+    L = _lib.lib()
+    fake = 0x10000  # 16-byte aligned, never dereferenced: every case fails validation first
+    # head_dim 64
+    st = L.dt_flash_fwd_qf32(None, None, None, None, 0, 128, None, None, None, 1, 16, 2, 64, 0.1, 1, None)
+    assert st == 4 and b"head_dim" in L.dt_last_error()
+    # null q
+    st = L.dt_flash_fwd_qf32(None, fake, fake, fake, 0, 256, None, None, None, 1, 16, 2, 128, 0.1, 1, None)
+    assert st == 1 and b"null" in L.dt_last_error()
+    # misaligned q
+    st = L.dt_flash_fwd_qf32(fake + 4, fake, fake, fake, 0, 256, None, None, None, 1, 16, 2, 128, 0.1, 1, None)
+    assert st == 1 and b"aligned" in L.dt_last_error()
+    # output row stride below H*D
+    st = L.dt_flash_fwd_qf32(fake, fake, fake, fake, 0, 128, None, None, None, 1, 16, 2, 128, 0.1, 1, None)
+    assert st == 1 and b"o_row_stride" in L.dt_last_error()
+    # empty problem: no-op success
+    assert L.dt_flash_fwd_qf32(None, None, None, None, 0, 256, None, None, None, 0, 16, 2, 128, 0.1, 1, None) == 0
+    bufs = (ctypes.c_void_p * 2)(fake, fake)
+    # rank out of range, token split that does not cover B*T
+    st = L.dt_flash_fwd_qf32_exchange(fake, fake, fake, bufs, 2, 2, 8, None, None, 1, 16, 2, 128, 0.1, 1, None)
+    assert st == 1 and b"rank" in L.dt_last_error()
+    st = L.dt_flash_fwd_qf32_exchange(fake, fake, fake, bufs, 2, 0, 7, None, None, 1, 16, 2, 128, 0.1, 1, None)
+    assert st == 1 and b"tokens_per_rank" in L.dt_last_error()
+
+
+def test_qf32_python_wrapper_rejects_host_tensors():
+    import pytest
+    import torch
+
+    import dirktensor_b200 as dt
+
+    q = torch.zeros((1, 16, 2, 128))
+    kb = torch.zeros((1, 16, 2, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="q must be"):
+        dt.flash_attention_forward_qf32(q, kb, kb, 0.1)
+
+
 def test_workspace_size():
     L = _lib.lib()
     n = 2 * 300 * 16 * 128
