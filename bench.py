@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -74,12 +75,12 @@ class ClockSampler:
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = None
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.fh = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix="dt_clocks_", suffix=".csv")
+            self.fh = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", self.gpu_id], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
@@ -112,6 +113,10 @@ class ClockSampler:
                 for n, v in zip(names, parts[5:9]):
                     if v.lower() == "active":
                         reasons.add(n)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
         loaded = [s for s, p in zip(sm, power) if p > 300] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
@@ -366,7 +371,7 @@ def main():
                        "flops_per_step": flops_step,
                        "l2": "inputs larger than L2 (805 MB fp32 per tensor in total)"},
             "prefill_tok_s": M / (ms_step * 1e-3),
-            "roofline": {"bound": "tensor", "kernel": "flash_fwd_kernel", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "tensor", "kernel": "attn_fwd_kernel", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": f"{src} bf16 burst",
                          "ms_per_launch": ms_flash, "flops_per_launch": f_flash_rank, "traffic": traffic},
             "cpu_baseline": cpu,

@@ -33,6 +33,9 @@ FlashAttentionGradients flash_attention_backward(const xt::xtensor<float, 4>& d_
     for (const auto* x : {&d_output, &output, &K, &V})
         if (x->shape() != Q.shape())
             throw std::invalid_argument("flash_attention_backward: d_output, output, Q, K, V shapes differ");
+    for (const auto* s : {&softmax_m, &softmax_l})
+        if (s->shape(0) != b || s->shape(1) != t || s->shape(2) != h)
+            throw std::invalid_argument("flash_attention_backward: softmax_m and softmax_l must be (batch, seq, n_heads)");
     FlashAttentionGradients g;
     g.d_Q = xt::empty<float>({b, t, h, d});
     g.d_K = xt::empty<float>({b, t, h, d});

@@ -3,6 +3,8 @@
 // project that uses the drop-in compiles it against the real xtensor instead;
 // the drop-in code relies only on API that both provide: shape(i), shape(),
 // size(), data(), operator(), and xt::empty / xt::zeros with a braced shape.
+// The element-wise sum of two tensors of one shape is here too, because the
+// reference's OlmoBlock (which holds the drop-in OlmoAttention) adds residuals.
 #pragma once
 
 #include <array>
@@ -48,6 +50,13 @@ private:
     shape_type dims_;
     std::vector<T> buf_;
 };
+
+template <class T, std::size_t N>
+xtensor<T, N> operator+(const xtensor<T, N>& a, const xtensor<T, N>& b) {
+    xtensor<T, N> r(a.shape());
+    for (std::size_t i = 0; i < r.size(); ++i) r.data()[i] = a.data()[i] + b.data()[i];
+    return r;
+}
 
 template <class T, std::size_t L>
 xtensor<T, L> empty(const std::size_t (&shape)[L]) {

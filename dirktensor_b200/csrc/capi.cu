@@ -153,9 +153,9 @@ struct DevState {
 std::mutex g_mu;
 DevState g_dev[64];
 
-constexpr size_t kFlashSmem = sizeof(dt::flash::Smem) + 1024;
-constexpr size_t kFlashBwdKvSmem = sizeof(dt::flash_bwd::SmemKV) + 1024;
-constexpr size_t kFlashBwdQSmem = sizeof(dt::flash_bwd::SmemQ) + 1024;
+constexpr size_t kFlashSmem = sizeof(dt::attn_fwd::Smem) + 1024;
+constexpr size_t kFlashBwdKvSmem = sizeof(dt::attn_bwd::SmemKV) + 1024;
+constexpr size_t kFlashBwdQSmem = sizeof(dt::attn_bwd::SmemQ) + 1024;
 constexpr size_t kGemmSmem = sizeof(dt::gemm::SmemT<dt::gemm::kBN>) + 1024;
 constexpr size_t kGemmNarrowSmem = sizeof(dt::gemm::SmemT<dt::gemm::kNarrowBN>) + 1024;
 constexpr size_t kGemm2Smem = sizeof(dt::gemm2::Smem) + 1024;
@@ -165,6 +165,27 @@ constexpr size_t kGemm2Smem = sizeof(dt::gemm2::Smem) + 1024;
 #ifndef DT_GEMM_2SM_MIN_M
 #define DT_GEMM_2SM_MIN_M 256
 #endif
+
+// Makes a handle's device current for the scope of an entry point and puts the
+// caller's current device back on every return path.
+class DeviceGuard {
+public:
+    int enter(int device) {
+        DT_CUDA(cudaGetDevice(&prev_));
+        if (prev_ != device) {
+            DT_CUDA(cudaSetDevice(device));
+            restore_ = true;
+        }
+        return DT_OK;
+    }
+    ~DeviceGuard() {
+        if (restore_) cudaSetDevice(prev_);
+    }
+
+private:
+    int prev_ = 0;
+    bool restore_ = false;
+};
 
 int current_device(int* dev) {
     DT_CUDA(cudaGetDevice(dev));
@@ -182,11 +203,11 @@ int ensure_attrs(int dev) {
         return fail(DT_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
                     prop.major, prop.minor);
     s.num_sms = prop.multiProcessorCount;
-    DT_CUDA(cudaFuncSetAttribute(dt::flash_bwd::flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    DT_CUDA(cudaFuncSetAttribute(dt::attn_bwd::attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kFlashBwdKvSmem));
-    DT_CUDA(cudaFuncSetAttribute(dt::flash_bwd::flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    DT_CUDA(cudaFuncSetAttribute(dt::attn_bwd::attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kFlashBwdQSmem));
-    DT_CUDA(cudaFuncSetAttribute(dt::flash::flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    DT_CUDA(cudaFuncSetAttribute(dt::attn_fwd::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kFlashSmem));
     DT_CUDA(cudaFuncSetAttribute(dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kBN>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
@@ -314,7 +335,7 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     DT_TRY(make_map_bthd(&mq, q_f32 ? k : q, B, T, H, 128));
     DT_TRY(make_map_bthd(&mk, k, B, T, H, 128));
     DT_TRY(make_map_bthd(&mv, v, B, T, H, 128));
-    dt::flash::Params p{};
+    dt::attn_fwd::Params p{};
     p.B = B;
     p.T = T;
     p.H = H;
@@ -355,7 +376,7 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     p.q_row_stride = (long long)H * 128;
     const long long grid = (long long)p.nblk * B * H;
     if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
-    dt::flash::flash_fwd_kernel<<<(unsigned)grid, dt::flash::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
+    dt::attn_fwd::attn_fwd_kernel<<<(unsigned)grid, dt::attn_fwd::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
     DT_CUDA(cudaGetLastError());
     return DT_OK;
 }
@@ -374,7 +395,7 @@ int launch_flash_bwd(const void* qb, const void* kb, const void* vb, const float
                      float* lse2, cudaStream_t st) {
     if ((long long)B * T * H == 0) return DT_OK;
     const int nblk = (T + 127) / 128;
-    dt::flash_bwd::PreParams pp{};
+    dt::attn_bwd::PreParams pp{};
     pp.out = out;
     pp.out_bf16 = reinterpret_cast<const __nv_bfloat16*>(out_bf16);
     pp.out_row_stride = out_row_stride;
@@ -389,14 +410,14 @@ int launch_flash_bwd(const void* qb, const void* kb, const void* vb, const float
     pp.H = H;
     pp.Tpad = nblk * 128;
     const long long rows = (long long)B * H * pp.Tpad;
-    dt::flash_bwd::flash_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(pp);
+    dt::attn_bwd::attn_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(pp);
     DT_CUDA(cudaGetLastError());
     CUtensorMap mq, mk, mv, mdo;
     DT_TRY(make_map_bthd(&mq, qb, B, T, H, 128));
     DT_TRY(make_map_bthd(&mk, kb, B, T, H, 128));
     DT_TRY(make_map_bthd(&mv, vb, B, T, H, 128));
     DT_TRY(make_map_bthd(&mdo, dob, B, T, H, 128));
-    dt::flash_bwd::Params p{};
+    dt::attn_bwd::Params p{};
     p.B = B;
     p.T = T;
     p.H = H;
@@ -412,10 +433,10 @@ int launch_flash_bwd(const void* qb, const void* kb, const void* vb, const float
     p.dv = dv;
     const long long grid = (long long)nblk * B * H;
     if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
-    dt::flash_bwd::flash_bwd_dkdv_kernel<<<(unsigned)grid, dt::flash_bwd::kThreads, kFlashBwdKvSmem, st>>>(
+    dt::attn_bwd::attn_bwd_dkdv_kernel<<<(unsigned)grid, dt::attn_bwd::kThreads, kFlashBwdKvSmem, st>>>(
         mq, mk, mv, mdo, p);
     DT_CUDA(cudaGetLastError());
-    dt::flash_bwd::flash_bwd_dq_kernel<<<(unsigned)grid, dt::flash_bwd::kThreads, kFlashBwdQSmem, st>>>(mq, mk, mv,
+    dt::attn_bwd::attn_bwd_dq_kernel<<<(unsigned)grid, dt::attn_bwd::kThreads, kFlashBwdQSmem, st>>>(mq, mk, mv,
                                                                                                       mdo, p);
     DT_CUDA(cudaGetLastError());
     return DT_OK;
@@ -748,13 +769,15 @@ int dt_flash_bwd_host(const float* dout, const float* out, const float* softmax_
 // host framework that forbids allocation from its callbacks, or a latency
 // critical loop where cudaMalloc/cudaFree (which can synchronise the device)
 // are not acceptable.  dt_flash_fwd needs a workspace for the bf16 copies of
-// Q, K and V; this variant keeps that workspace in a fixed array that is part
-// of the library's device image, so a call allocates nothing.
+// K and V; this variant keeps that workspace in a fixed array that is part of
+// the library's device image, so a call allocates nothing.  Q is read as fp32
+// and rounded inside the attention kernel, exactly as dt_flash_fwd does, so
+// the two entry points return bit-identical results.
 //
 // Limits and behaviour:
 //  * The array is kNoAllocScratchBytes (24 MiB) on every GPU that loads the
-//    library, held until the process exits.  It fits B*T*H*D <= 4,194,304
-//    elements (for example B=1, T=2048, H=16, D=128); larger problems are
+//    library, held until the process exits.  It fits B*T*H*D <= 6,291,456
+//    elements (for example B=1, T=3072, H=16, D=128); larger problems are
 //    rejected with DT_ERR_INVALID_ARGUMENT before anything is launched.
 //  * All calls on a device share the one array, and it keeps whatever the last
 //    call wrote.  Nothing in it has to start at zero (each call overwrites the
@@ -762,15 +785,20 @@ int dt_flash_bwd_host(const float* dout, const float* out, const float* softmax_
 //    on the GPU (different streams, no ordering between them) race on it; order
 //    them on one stream or with events.
 //  * The first call on a device, with that device current, looks up the
-//    array's device address (cudaGetSymbolAddress) and caches it.  Make that
-//    first call before any stream capture.
+//    array's device address (cudaGetSymbolAddress) and caches it for the rest
+//    of the process.  Make that first call before any stream capture.  The
+//    cache assumes the device's primary context is never reset: after
+//    cudaDeviceReset the cached address is stale, so do not call this entry
+//    point again in a process that reset the device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[24u << 20];
 constexpr size_t kNoAllocScratchBytes = sizeof(g_noalloc_scratch);
 
 namespace {
-void* g_noalloc_addr[64] = {};
+constexpr int kMaxDevices = 64;
+void* g_noalloc_addr[kMaxDevices] = {};
 
 int noalloc_scratch(int dev, void** out) {
+    if (dev < 0 || dev >= kMaxDevices) return fail(DT_ERR_UNSUPPORTED, "device index %d out of range", dev);
     std::lock_guard<std::mutex> lk(g_mu);
     if (g_noalloc_addr[dev] == nullptr) {
         void* ptr = nullptr;
@@ -794,20 +822,21 @@ int dt_flash_fwd_noalloc(const float* q, const float* k, const float* v, float* 
         return fail(DT_ERR_INVALID_ARGUMENT, "q/k/v/o must be 16-byte aligned");
     const long long n = (long long)B * T * H * D;
     const size_t one = align256((size_t)n * 2);
-    if (3 * one > kNoAllocScratchBytes)
+    if (2 * one > kNoAllocScratchBytes)
         return fail(DT_ERR_INVALID_ARGUMENT,
                     "dt_flash_fwd_noalloc: B*T*H*D = %lld exceeds the fixed scratch (at most %zu elements); "
                     "use dt_flash_fwd with a caller workspace",
-                    n, kNoAllocScratchBytes / 6);
+                    n, kNoAllocScratchBytes / 4);
     int dev;
     DT_TRY(prepare_device(&dev));
     void* scratch;
     DT_TRY(noalloc_scratch(dev, &scratch));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     uint8_t* ws = reinterpret_cast<uint8_t*>(scratch);
-    DT_TRY(launch_cast3(q, k, v, ws, ws + one, ws + 2 * one, n, st));
-    return launch_flash(ws, ws + one, ws + 2 * one, o, 0, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H,
-                        scale, causal, st);
+    // K and V to bf16 in the fixed scratch; the attention kernel reads the fp32 Q rows itself
+    DT_TRY(launch_cast3(k, v, nullptr, ws, ws + one, nullptr, n, st, 2));
+    return launch_flash(nullptr, ws, ws + one, o, 0, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale,
+                        causal, st, Scatter(), q);
 }
 
 int dt_flash_fwd_bf16(const void* q, const void* k, const void* v, void* o, int o_bf16, long long o_row_stride,
@@ -1072,7 +1101,8 @@ int dt_attn_create(const dt_attn_weights* w, int device, dt_attn** out) {
     if (w->d_model != 2048 || w->n_heads <= 0 || w->d_model % w->n_heads != 0 || w->d_model / w->n_heads != 128)
         return fail(DT_ERR_UNSUPPORTED, "need d_model 2048 and head_dim 128 (got d_model=%d n_heads=%d)", w->d_model,
                     w->n_heads);
-    DT_CUDA(cudaSetDevice(device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(device));
     int dev;
     DT_TRY(prepare_device(&dev));
     dt_attn* a = new dt_attn();
@@ -1255,9 +1285,8 @@ int dt_attn_forward(dt_attn* a, const float* x, int B, int T, const int* seq_len
     const long long M = (long long)B * T;
     if (M == 0) return DT_OK;
     if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(DT_ERR_INVALID_ARGUMENT, "x/y must be 16-byte aligned");
-    int cur;
-    DT_CUDA(cudaGetDevice(&cur));
-    if (cur != a->device) DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     int dev;
     DT_TRY(prepare_device(&dev));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1279,7 +1308,8 @@ int dt_attn_forward_host(dt_attn* a, const float* x, int B, int T, const int* se
     const long long M = (long long)B * T;
     if (M == 0) return DT_OK;
     if (!x || !y) return fail(DT_ERR_INVALID_ARGUMENT, "null x/y");
-    DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     if (!a->stream) DT_CUDA(cudaStreamCreateWithFlags(&a->stream, cudaStreamNonBlocking));
     const size_t xb = align256((size_t)M * a->d_model * 4);
     const size_t need = 2 * xb + align256((size_t)B * 4);
@@ -1334,7 +1364,8 @@ int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void*
         return fail(DT_ERR_UNSUPPORTED, "backward of a forward with seq_lens (the reference has no padding mask)");
     if (!dy || !dx || !aligned16(dy) || !aligned16(dx))
         return fail(DT_ERR_INVALID_ARGUMENT, "dy/dx must be non-null and 16-byte aligned");
-    DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     int dev;
     DT_TRY(prepare_device(&dev));
     DT_TRY(attn_grads(a));
@@ -1420,7 +1451,8 @@ int dt_attn_backward_host(dt_attn* a, const float* dy, int B, int T, float* dx) 
     if (M <= 0 || B != a->last_B || T != a->last_T)
         return fail(DT_ERR_INVALID_ARGUMENT, "backward needs the shape of the last forward (B=%d T=%d)", a->last_B,
                     a->last_T);
-    DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     if (!a->stream) DT_CUDA(cudaStreamCreateWithFlags(&a->stream, cudaStreamNonBlocking));
     const size_t xb = align256((size_t)M * a->d_model * 4);
     if (a->io_bytes < 2 * xb) {
@@ -1444,7 +1476,8 @@ int dt_attn_backward_host(dt_attn* a, const float* dy, int B, int T, float* dx) 
 int dt_attn_step(dt_attn* a, float lr, void* stream) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
-    DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     DT_TRY(attn_grads(a));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const long long dd = (long long)a->d_model * a->d_model;
@@ -1459,7 +1492,8 @@ int dt_attn_step(dt_attn* a, float lr, void* stream) {
 int dt_attn_zero_grad(dt_attn* a, void* stream) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
-    DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     if (!a->grad) return DT_OK;
     const size_t d = (size_t)a->d_model;
     DT_CUDA(cudaMemsetAsync(a->grad, 0, (4 * d * d + 2 * d) * 4, reinterpret_cast<cudaStream_t>(stream)));
@@ -1470,7 +1504,8 @@ int dt_attn_get_params_host(dt_attn* a, float* q_proj, float* k_proj, float* v_p
                             float* k_norm, int gradients) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
-    DT_CUDA(cudaSetDevice(a->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
     DT_CUDA(cudaDeviceSynchronize());
     const size_t d = (size_t)a->d_model, dd = d * d;
     if (gradients) DT_TRY(attn_grads(a));
@@ -1611,7 +1646,8 @@ int dt_model_create(const dt_model_weights* w, int device, dt_model** out) {
             !L.gate_proj || !L.up_proj || !L.down_proj || !L.post_feedforward_norm)
             return fail(DT_ERR_INVALID_ARGUMENT, "null weight pointer in layer %d", l);
     }
-    DT_CUDA(cudaSetDevice(device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(device));
     int dev;
     DT_TRY(prepare_device(&dev));
     dt_model* m = new dt_model();
@@ -1698,7 +1734,8 @@ int dt_model_forward(dt_model* m, const uint32_t* tokens, int B, int T, float* l
     const long long M = (long long)B * T;
     if (M == 0) return DT_OK;
     if (!tokens || !logits || !aligned16(logits)) return fail(DT_ERR_INVALID_ARGUMENT, "tokens/logits invalid");
-    DT_CUDA(cudaSetDevice(m->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(m->device));
     int dev;
     DT_TRY(prepare_device(&dev));
     const size_t need = model_ws_bytes(m, M);
@@ -1760,7 +1797,8 @@ int dt_model_forward_host(dt_model* m, const uint32_t* tokens, int B, int T, flo
         if (tokens[i] >= (uint32_t)m->vocab)
             return fail(DT_ERR_INVALID_ARGUMENT, "token id %u at position %lld is not below the vocabulary size %d",
                         tokens[i], i, m->vocab);
-    DT_CUDA(cudaSetDevice(m->device));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(m->device));
     if (!m->stream) DT_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     const size_t lb = align256((size_t)M * m->vocab * 4);
     const size_t need = lb + align256((size_t)M * 4);

@@ -8,14 +8,14 @@
 //   dP = dO V^T,   D = rowsum(O * dO),   dS = P * (dP - D) * scale
 //   dV = P^T dO,   dK = dS^T Q,   dQ = dS K.
 // Three kernels:
-//   flash_bwd_pre_kernel   D, lse2 = m*log2(e) + log2(l) per row ([B, H, Tpad],
+//   attn_bwd_pre_kernel   D, lse2 = m*log2(e) + log2(l) per row ([B, H, Tpad],
 //                          +inf / 0 in the padding rows), and a bf16 copy of dO;
-//   flash_bwd_dkdv_kernel  one CTA per (b, h, 128-key block), K and V resident,
+//   attn_bwd_dkdv_kernel  one CTA per (b, h, 128-key block), K and V resident,
 //                          looping over the 128-query blocks that see the keys:
 //                          S^T = K Q^T and dP^T = V dO^T into TMEM, P^T and dS^T
 //                          written back over them as bf16, then dV += P^T dO and
 //                          dK += dS^T Q accumulate in TMEM (512 columns);
-//   flash_bwd_dq_kernel    one CTA per (b, h, 128-query block), Q and dO resident,
+//   attn_bwd_dq_kernel    one CTA per (b, h, 128-query block), Q and dO resident,
 //                          looping over key blocks: S = Q K^T, dP = dO V^T,
 //                          dS over dP, dQ += dS K in TMEM.
 // Splitting dQ from dK/dV costs two extra products per tile pair (S and dP are
@@ -26,7 +26,7 @@
 #include "dt_common.cuh"
 
 namespace dt {
-namespace flash_bwd {
+namespace attn_bwd {
 
 constexpr int kD = 128;
 constexpr int kBM = 128;  // rows of a Q or K/V block
@@ -58,7 +58,7 @@ struct PreParams {
     int B, T, H, Tpad;
 };
 
-__global__ void __launch_bounds__(256) flash_bwd_pre_kernel(const PreParams p) {
+__global__ void __launch_bounds__(256) attn_bwd_pre_kernel(const PreParams p) {
     const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const long long nrows = (long long)p.B * p.H * p.Tpad;
@@ -182,7 +182,7 @@ struct __align__(1024) SmemKV {
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
-flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                       const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_do,
                       const Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -478,7 +478,7 @@ static_assert(sizeof(SmemQ) + 1024 <= 232448, "dq kernel shared memory exceeds 2
 static_assert(sizeof(SmemKV) + 1024 <= 232448, "dkdv kernel shared memory exceeds 227 KB");
 
 __global__ void __launch_bounds__(kThreads, 1)
-flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_do,
                     const Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -693,5 +693,5 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     }
 }
 
-}  // namespace flash_bwd
+}  // namespace attn_bwd
 }  // namespace dt

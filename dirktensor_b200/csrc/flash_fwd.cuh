@@ -32,7 +32,7 @@
 #include "dt_common.cuh"
 
 namespace dt {
-namespace flash {
+namespace attn_fwd {
 
 constexpr int kD = 128;
 constexpr int kBM = 128;
@@ -134,7 +134,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -504,5 +504,5 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     }
 }
 
-}  // namespace flash
+}  // namespace attn_fwd
 }  // namespace dt

@@ -91,15 +91,17 @@ int dt_flash_bwd_host(const float* dout, const float* out, const float* softmax_
                       int H, int D, float scale, int causal);
 
 /* Same as dt_flash_fwd, but allocates nothing and takes no workspace: the
- * bf16 operand copies live in a fixed 24 MiB array inside the library's device
- * image (present on every GPU that loads the library until exit).  No
- * counterpart in the reference: it exists for callers that cannot allocate
- * device memory (an engine that owns its whole HBM budget through its own
- * pool, a plugin barred from allocating in callbacks, a loop that cannot
- * afford cudaMalloc's synchronisation).  B*T*H*D must be <= 4,194,304, else
- * DT_ERR_INVALID_ARGUMENT.  All calls share the array: calls that may overlap
- * on the GPU race and must be ordered by the caller.  The first call on a
- * device looks up the array's address; make it before any stream capture. */
+ * bf16 copies of K and V live in a fixed 24 MiB array inside the library's
+ * device image (present on every GPU that loads the library until exit); Q is
+ * rounded inside the attention kernel, so results are bit-identical to
+ * dt_flash_fwd's.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory (an engine that owns its whole HBM budget
+ * through its own pool, a plugin barred from allocating in callbacks, a loop
+ * that cannot afford cudaMalloc's synchronisation).  B*T*H*D must be
+ * <= 6,291,456, else DT_ERR_INVALID_ARGUMENT.  All calls share the array:
+ * calls that may overlap on the GPU race and must be ordered by the caller.
+ * The first call on a device looks up the array's address and caches it; make
+ * it before any stream capture, and do not call again after cudaDeviceReset. */
 int dt_flash_fwd_noalloc(const float* q, const float* k, const float* v, float* o, float* softmax_m,
                          float* softmax_l, int B, int T, int H, int D, float scale, int causal, void* stream);
 

@@ -29,11 +29,25 @@ _lib = None
 _ref = None
 
 
+def reference_dir() -> str:
+    """The reference source tree: $DT_REFERENCE_DIR, else the Makefile's REF default."""
+    env = os.environ.get("DT_REFERENCE_DIR")
+    if env:
+        return env
+    r = subprocess.run(["make", "-s", "-C", HERE, "print-ref"], capture_output=True, text=True)
+    return r.stdout.strip()
+
+
+def reference_present() -> bool:
+    d = reference_dir()
+    return bool(d) and os.path.exists(os.path.join(d, "FlashAttention.cpp"))
+
+
 def build(with_reference: bool | None = None) -> None:
     """Build liboracle.so, and the reference library when its sources exist."""
     targets = ["oracle"]
     if with_reference is None:
-        with_reference = os.path.exists("/root/reference/FlashAttention.cpp")
+        with_reference = reference_present()
     if with_reference:
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)

@@ -53,3 +53,25 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
     u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
     return u.astype(np.uint32).view(np.float32)
+
+
+def model_layer_weights(seed: int, d: int = 2048, hidden: int = 8192):
+    """One OLMo-2 block's weights (config 3): projections N(0, 0.02), norm gains 1 + N(0, 0.02)."""
+    shapes = {"q_proj": (d, d), "k_proj": (d, d), "v_proj": (d, d), "o_proj": (d, d), "gate_proj": (hidden, d),
+              "up_proj": (hidden, d), "down_proj": (d, hidden)}
+    w = {k: randn(seed * 31 + i, s, 0.02) for i, (k, s) in enumerate(shapes.items())}
+    for i, k in enumerate(("q_norm", "k_norm", "post_attention_norm", "post_feedforward_norm")):
+        w[k] = (1 + randn(seed * 31 + 20 + i, (d,), 0.02)).astype(np.float32)
+    return w
+
+
+def model_weights(seed: int, n_layers: int, vocab: int, distinct: int = 2):
+    """Embedding, blocks, final norm gain and LM head.  `distinct` weight sets are
+    generated and repeated over the layers (generation time, not arithmetic,
+    is what this saves)."""
+    base = [model_layer_weights(seed + i) for i in range(min(distinct, n_layers))]
+    layers = [base[i % len(base)] for i in range(n_layers)]
+    embed = randn(seed + 100, (vocab, 2048), 0.02)
+    lm_head = randn(seed + 101, (vocab, 2048), 0.02)
+    final_norm = (1 + randn(seed + 102, (2048,), 0.02)).astype(np.float32)
+    return embed, layers, final_norm, lm_head

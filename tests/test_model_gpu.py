@@ -6,30 +6,12 @@ import numpy as np
 import pytest
 
 import oracle
-from common import randn, rel_l2
+from common import model_weights, rel_l2
 
 pytestmark = pytest.mark.gpu
 
 TOL_LOGITS_REL_L2 = 3e-2
 KEYS = oracle.LAYER_KEYS
-
-
-def layer(seed, d=2048, hidden=8192):
-    shapes = {"q_proj": (d, d), "k_proj": (d, d), "v_proj": (d, d), "o_proj": (d, d), "gate_proj": (hidden, d),
-              "up_proj": (hidden, d), "down_proj": (d, hidden)}
-    w = {k: randn(seed * 31 + i, s, 0.02) for i, (k, s) in enumerate(shapes.items())}
-    for i, k in enumerate(("q_norm", "k_norm", "post_attention_norm", "post_feedforward_norm")):
-        w[k] = (1 + randn(seed * 31 + 20 + i, (d,), 0.02)).astype(np.float32)
-    return w
-
-
-def model_weights(seed, n_layers, vocab, distinct=2):
-    base = [layer(seed + i) for i in range(min(distinct, n_layers))]
-    layers = [base[i % len(base)] for i in range(n_layers)]
-    embed = randn(seed + 100, (vocab, 2048), 0.02)
-    lm_head = randn(seed + 101, (vocab, 2048), 0.02)
-    final_norm = (1 + randn(seed + 102, (2048,), 0.02)).astype(np.float32)
-    return embed, layers, final_norm, lm_head
 
 
 def compare(cuda, n_layers, vocab, B, T, seed):
