@@ -10,6 +10,7 @@ from .attention import (  # noqa: F401
     OlmoAttention,
     OlmoModel,
     cast_bf16,
+    cast2_bf16,
     check_device_error,
     d_model,
     flash_attention_backward,

@@ -118,6 +118,7 @@ SIGNATURES = {
     "dt_model_destroy": (_I, [_P]),
     "dt_model_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "dt_cast_f32_bf16": (_I, [_P, _P, _LL, _P]),
+    "dt_cast2_f32_bf16": (_I, [_P, _P, _P, _P, _LL, _P]),
     "dt_gemm_bf16_tn": (_I, [_P, _P, _P, _I, _I, _I, _I, _LL, _P]),
     "dt_gemm_bf16_tn_planar": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _LL, _P]),
     "dt_qk_norm_rope": (_I, [_P, _P, _P, _LL, _P, _P, _P, _P, _P, _I, _I, _F, _F, _P]),

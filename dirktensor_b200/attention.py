@@ -209,6 +209,20 @@ def cast_bf16(x):
     return y
 
 
+def cast2_bf16(x, y):
+    """bf16 copies of two float32 CUDA tensors of one element count, in one launch."""
+    torch = _torch()
+    _need_cuda_f32("x", x, x.dim())
+    _need_cuda_f32("y", y, y.dim())
+    if x.numel() != y.numel():
+        raise ValueError("x and y must have the same number of elements")
+    xb = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    yb = torch.empty(y.shape, dtype=torch.bfloat16, device=y.device)
+    check(lib().dt_cast2_f32_bf16(x.data_ptr(), y.data_ptr(), xb.data_ptr(), yb.data_ptr(), x.numel(),
+                                  _stream_ptr(x.device)))
+    return xb, yb
+
+
 def gemm_bf16_tn(A, B, out_bf16: bool = False, out=None):
     """C = A . B^T with A [M, K], B [N, K] bf16 CUDA tensors."""
     torch = _torch()

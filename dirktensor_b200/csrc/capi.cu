@@ -986,6 +986,16 @@ int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream) {
     return launch_cast(src, dst, n, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int dt_cast2_f32_bf16(const float* src0, const float* src1, void* dst0, void* dst1, long long n, void* stream) {
+    t_last_error.clear();
+    if (n < 0 || (n % 4) != 0) return fail(DT_ERR_INVALID_ARGUMENT, "n must be a non-negative multiple of 4");
+    if (n == 0) return DT_OK;
+    if (!src0 || !src1 || !dst0 || !dst1 || !aligned16(src0) || !aligned16(src1) || ((uintptr_t)dst0 & 7u) ||
+        ((uintptr_t)dst1 & 7u))
+        return fail(DT_ERR_INVALID_ARGUMENT, "sources must be 16-byte and destinations 8-byte aligned");
+    return launch_cast3(src0, src1, nullptr, dst0, dst1, nullptr, n, reinterpret_cast<cudaStream_t>(stream), 2);
+}
+
 int dt_gemm_bf16_tn(const void* A, const void* B, void* C, int c_bf16, int M, int N, int K, long long ldc,
                     void* stream) {
     t_last_error.clear();

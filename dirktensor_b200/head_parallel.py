@@ -26,7 +26,7 @@ Two exchange modes:
       instruction to the peer; one system-scope fence kernel after the
       attention kernel (not one fence per storing thread) publishes the stores.
       The attention kernel reads this rank's Q in fp32 and rounds it itself
-      (K and V are cast first).  Measured at 2 GPUs (config 4): 1.70 ms per
+      (K and V are cast first, in one launch).  Measured at 2 GPUs (config 4): 1.70 ms per
       step; 2.09 ms for the NCCL path.
   nccl: the flash kernel writes a local [M, Hl*D] buffer and
       torch.distributed.all_to_all_single moves the token slices.
@@ -98,7 +98,7 @@ class HeadParallelAttention:
     def local_attention(self, q, k, v, scale: float, causal: bool, events=None) -> torch.Tensor:
         """Flash attention on this rank's heads -> bf16 [M, Hl*D]."""
         B, T, Hl, D = q.shape
-        kb, vb = (_attn.cast_bf16(t) for t in (k, v))  # the attention kernel rounds q itself
+        kb, vb = _attn.cast2_bf16(k.contiguous(), v.contiguous())  # the attention kernel rounds q itself
         out = self._buf("o_local", (B * T, Hl * D), torch.bfloat16, q.device)
         if events is not None:
             events[0].record()
@@ -108,11 +108,18 @@ class HeadParallelAttention:
             events[1].record()
         return out
 
-    def project(self, a: torch.Tensor, planes: int) -> torch.Tensor:
-        """y = A . Wo^T for A planar over `planes` planes ([planes, m, K/planes])."""
+    def project(self, a: torch.Tensor, planes: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y = A . Wo^T for A planar over `planes` planes ([planes, m, K/planes]).
+        `out` ([m, d] float32, contiguous) receives y; by default a buffer that
+        the next call reuses."""
         m = a.shape[1] if planes > 1 else a.shape[0]
         d = self.wo.shape[0]
-        y = self._buf("y", (m, d), torch.float32, a.device)
+        if out is None:
+            y = self._buf("y", (m, d), torch.float32, a.device)
+        else:
+            if out.shape != (m, d) or out.dtype != torch.float32 or not out.is_contiguous():
+                raise ValueError(f"out must be a contiguous float32 [{m}, {d}] tensor")
+            y = out
         K = self.wo.shape[1]
         stream = torch.cuda.current_stream(a.device).cuda_stream
         if planes > 1:
@@ -187,7 +194,7 @@ class HeadParallelAttention:
         self._setup_fused(M, Hl * D, q.device)
         buf = self._step & 1
         self._step += 1
-        kb, vb = (_attn.cast_bf16(t) for t in (k, v))  # the attention kernel rounds q itself
+        kb, vb = _attn.cast2_bf16(k.contiguous(), v.contiguous())  # the attention kernel rounds q itself
         q = q.contiguous()
         if events is not None:
             events[0].record()
@@ -201,7 +208,8 @@ class HeadParallelAttention:
         dist.all_reduce(self._barrier, group=self.group)
         return self._fused[1][buf]
 
-    def forward(self, q, k, v, scale: float, causal: bool = True, events=None) -> torch.Tensor:
+    def forward(self, q, k, v, scale: float, causal: bool = True, events=None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, T, Hl, D = q.shape
         if Hl != self.h1 - self.h0 or D != self.head_dim:
             raise ValueError(f"expected [B, T, {self.h1 - self.h0}, {self.head_dim}] local heads")
@@ -211,6 +219,6 @@ class HeadParallelAttention:
         else:
             o_local = self.local_attention(q, k, v, scale, causal, events)
             a = self.exchange(o_local)
-        return self.project(a, self.world)
+        return self.project(a, self.world, out)
 
     __call__ = forward

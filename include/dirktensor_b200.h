@@ -248,6 +248,9 @@ int dt_model_info(const dt_model* m, int* n_layers, int* vocab, int* hidden);
 /* ---- stages (for stage-wise parity checks and head-sharded callers) ----- */
 /* dst[i] = bf16(src[i]), n elements (n % 4 == 0). */
 int dt_cast_f32_bf16(const float* src, void* dst, long long n, void* stream);
+/* dst0 = bf16(src0) and dst1 = bf16(src1), n elements each (n % 4 == 0), in one
+ * launch (the K and V operands of the head-parallel attention step). */
+int dt_cast2_f32_bf16(const float* src0, const float* src1, void* dst0, void* dst1, long long n, void* stream);
 /* C[M,N] = A[M,K] . B[N,K]^T; A, B bf16 row-major device; C fp32 (c_bf16 = 0)
  * or bf16 (c_bf16 = 1) with ldc elements per row.  K % 8 == 0.
  * The projection products of OlmoAttention.cpp:68,74,80,103-105. */

@@ -40,9 +40,13 @@ def _worker(rank, world, port, B, T, H, out_dir):
             Bq, Tq, Hl, D = q.shape
             return torch.from_numpy(o.reshape(Bq * Tq, Hl * D))
 
-        def project(self, a, planes):
+        def project(self, a, planes, out=None):
             A = a.permute(1, 0, 2).reshape(a.shape[1], -1) if planes > 1 else a
-            return torch.from_numpy(oracle.linear(A.contiguous().numpy(), self.wo.numpy()))
+            y = torch.from_numpy(oracle.linear(A.contiguous().numpy(), self.wo.numpy()))
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
 
     q, k, v = qkv(5, B, T, H)
     wo = randn(6, (2048 // 16 * H, 2048 // 16 * H), 0.02)

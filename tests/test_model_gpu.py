@@ -46,6 +46,47 @@ def test_model_full_architecture_16_layers(cuda):
     assert np.isfinite(got).all()
 
 
+def test_model_config3_full_size(cuda):
+    """Configuration 3 at its stated size: B=4, T=4096, 16 layers, d_model 2048,
+    SwiGLU 8192, vocab 100352, token ids uniform in [0, 100278), weights
+    N(0, 0.02) (four distinct random layer sets, each used by four layers) and
+    norm gains 1 + N(0, 0.02).  The GPU logits of all four sequences are compared
+    with the oracle's restatement of OlmoModel::forward (OlmoModel.cpp:25-48),
+    run one sequence at a time on the host (sequences are independent; the
+    reference's saved activations for the whole batch would not fit host RAM).
+    Tolerance: relative L2 <= 3e-2 per sequence and over the batch; top-1
+    agreement >= 0.95 (measured values are printed)."""
+    import torch
+
+    import dirktensor_b200 as dt
+
+    B, T, n_layers, vocab = 4, 4096, 16, 100352
+    embed, layers, final_norm, lm_head = model_weights(301, n_layers, vocab, distinct=4)
+    ids = np.random.default_rng(301).integers(0, 100278, (B, T)).astype(np.uint32)
+    m = dt.OlmoModel.from_weights(embed, layers, final_norm, lm_head)
+    got = m.forward(torch.from_numpy(ids.astype(np.int32)).to(cuda)).cpu().numpy()
+    dt.check_device_error()
+    m.close()
+    assert got.shape == (B, T, vocab) and np.isfinite(got).all()
+    num = den = 0.0
+    agree = []
+    for b in range(B):
+        ref = oracle.model_forward(ids[b:b + 1], embed, layers, final_norm, lm_head)[0]
+        g = got[b]
+        e = rel_l2(g, ref)
+        top1 = float(np.mean(g.argmax(-1) == ref.argmax(-1)))
+        print(f"config3 sequence {b}: rel-L2 {e:.3e}, max abs {np.max(np.abs(g - ref)):.3e}, top-1 {top1:.4f}")
+        assert e < TOL_LOGITS_REL_L2, (b, e)
+        d = np.asarray(g, np.float64) - ref
+        num += float(np.sum(d * d))
+        den += float(np.sum(np.asarray(ref, np.float64) ** 2))
+        agree.append(top1)
+    err = (num / den) ** 0.5
+    print(f"config3 B=4 T=4096: rel-L2 {err:.3e}, top-1 agreement {np.mean(agree):.4f}")
+    assert err < TOL_LOGITS_REL_L2, err
+    assert np.mean(agree) >= 0.95, agree
+
+
 def test_model_rejects_out_of_range_tokens(cuda):
     import dirktensor_b200 as dt
 
