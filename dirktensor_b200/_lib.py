@@ -22,6 +22,8 @@ STATUS_NAMES = {
     4: "DT_ERR_UNSUPPORTED",
     5: "DT_ERR_OUT_OF_MEMORY",
     6: "DT_ERR_IO",
+    7: "DT_ERR_NCCL",
+    8: "DT_ERR_TIMEOUT",
 }
 
 
@@ -123,6 +125,14 @@ SIGNATURES = {
     "dt_gemm_bf16_tn_planar": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _LL, _P]),
     "dt_qk_norm_rope": (_I, [_P, _P, _P, _LL, _P, _P, _P, _P, _P, _I, _I, _F, _F, _P]),
     "dt_rope_tables": (_I, [_P, _P, _I, _I, _F]),
+    "dt_qk_sumsq": (_I, [_P, _P, _LL, _I, _LL, _P, _P]),
+    "dt_qk_norm_rope_shard": (_I, [_P, _P, _P, _LL, _P, _P, _P, _I, _P, _P, _P, _I, _I, _F, _F, _P]),
+    "dt_comm_unique_id": (_I, [_P]),
+    "dt_comm_create": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_P)]),
+    "dt_comm_abort": (_I, [_P]),
+    "dt_comm_destroy": (_I, [_P]),
+    "dt_attn_create_sharded": (_I, [ctypes.POINTER(dt_attn_weights), _P, _I, ctypes.POINTER(_P)]),
+    "dt_attn_forward_sharded": (_I, [_P, _P, _I, _I, _P, _P, _P]),
 }
 
 

@@ -3,13 +3,17 @@
 // the kernel headers are included below.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -540,6 +544,45 @@ int launch_prologue(const float* q, const float* k, const float* v, long long ld
     return DT_OK;
 }
 
+int launch_sumsq(const float* q, const float* k, long long ld, int width, long long M, float* ss, cudaStream_t st) {
+    if (M == 0) return DT_OK;
+    const long long blocks = (M + 7) / 8;
+    if (blocks > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "too many rows");
+    dt::elem::qk_sumsq_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, k, ld, width, M, reinterpret_cast<float2*>(ss));
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int launch_prologue_shard(const float* q, const float* k, const float* v, long long ld_in, const float* ss,
+                          const float* qg, const float* kg, int heads, const float* sin_t, const float* cos_t,
+                          void* qo, void* ko, void* vo, int B, int T, float eps, cudaStream_t st) {
+    const long long M = (long long)B * T;
+    if (M == 0) return DT_OK;
+    dt::elem::ShardPrologueParams p;
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.ld_in = ld_in;
+    p.ss = reinterpret_cast<const float2*>(ss);
+    p.q_gain = qg;
+    p.k_gain = kg;
+    p.sin_t = sin_t;
+    p.cos_t = cos_t;
+    p.qo = reinterpret_cast<__nv_bfloat16*>(qo);
+    p.ko = reinterpret_cast<__nv_bfloat16*>(ko);
+    p.vo = reinterpret_cast<__nv_bfloat16*>(vo);
+    p.heads = heads;
+    p.T = T;
+    p.M = M;
+    p.eps = eps;
+    const int per_cta = dt::elem::kPrologueThreads / (heads * 16);
+    const long long blocks = (M + per_cta - 1) / per_cta;
+    if (blocks > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "too many rows");
+    dt::elem::qk_norm_rope_shard_kernel<<<(unsigned)blocks, dt::elem::kPrologueThreads, 0, st>>>(p);
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
 int check_flash_shape(int B, int T, int H, int D) {
     if (B < 0 || T < 0 || H < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape B=%d T=%d H=%d", B, T, H);
     if (D != 128) return fail(DT_ERR_UNSUPPORTED, "head_dim %d unsupported (must be 128)", D);
@@ -560,6 +603,132 @@ int read_device_error(bool* had) {
     return DT_OK;
 }
 
+}  // namespace
+
+// ===========================================================================
+// NCCL, loaded at run time (the single-GPU entry points need no NCCL)
+// ===========================================================================
+namespace {
+struct NcclApi {
+    bool loaded = false;
+    std::string err;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl_api() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            const char* e = dlerror();
+            api.err = e ? e : "dlopen(libnccl.so.2) failed";
+            return;
+        }
+#define DT_NCCL_SYM(field, sym)                                              \
+    api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, sym));        \
+    if (!api.field) {                                                        \
+        api.err = std::string("libnccl.so.2 has no ") + sym;                 \
+        return;                                                              \
+    }
+        DT_NCCL_SYM(GetUniqueId, "ncclGetUniqueId")
+        DT_NCCL_SYM(CommInitRankConfig, "ncclCommInitRankConfig")
+        DT_NCCL_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
+        DT_NCCL_SYM(CommAbort, "ncclCommAbort")
+        DT_NCCL_SYM(CommDestroy, "ncclCommDestroy")
+        DT_NCCL_SYM(AllReduce, "ncclAllReduce")
+        DT_NCCL_SYM(AllGather, "ncclAllGather")
+        DT_NCCL_SYM(Send, "ncclSend")
+        DT_NCCL_SYM(Recv, "ncclRecv")
+        DT_NCCL_SYM(GroupStart, "ncclGroupStart")
+        DT_NCCL_SYM(GroupEnd, "ncclGroupEnd")
+        DT_NCCL_SYM(GetErrorString, "ncclGetErrorString")
+#undef DT_NCCL_SYM
+        api.loaded = true;
+    });
+    return api;
+}
+
+int need_nccl(NcclApi** out) {
+    NcclApi& n = nccl_api();
+    if (!n.loaded) return fail(DT_ERR_NCCL, "NCCL unavailable: %s", n.err.c_str());
+    *out = &n;
+    return DT_OK;
+}
+}  // namespace
+
+struct dt_comm {
+    ncclComm_t comm = nullptr;
+    int world = 1, rank = 0, device = 0;
+    int timeout_ms = 60000;
+};
+
+namespace {
+// The communicator is non-blocking: a call may return ncclInProgress while
+// NCCL finishes it in the background.  Polls until it is done, giving up
+// (and aborting the communicator) after the communicator's timeout.
+int nccl_done(dt_comm* c, ncclResult_t r, const char* what) {
+    NcclApi& n = nccl_api();
+    if (r == ncclInProgress) {
+        const auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+            ncclResult_t st = ncclSuccess;
+            const ncclResult_t q = n.CommGetAsyncError(c->comm, &st);
+            if (q != ncclSuccess) {
+                r = q;
+                break;
+            }
+            if (st != ncclInProgress) {
+                r = st;
+                break;
+            }
+            const auto ms =
+                std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+            if (ms > c->timeout_ms) {
+                n.CommAbort(c->comm);
+                c->comm = nullptr;
+                return fail(DT_ERR_TIMEOUT, "%s did not complete within %d ms; the communicator was aborted", what,
+                            c->timeout_ms);
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(100));
+        }
+    }
+    if (r != ncclSuccess) return fail(DT_ERR_NCCL, "%s: %s", what, n.GetErrorString(r));
+    return DT_OK;
+}
+
+int comm_ok(dt_comm* c) {
+    if (!c || !c->comm) return fail(DT_ERR_INVALID_ARGUMENT, "communicator is null or was aborted");
+    return DT_OK;
+}
+
+// State of a head-sharded attention handle (dt_attn_create_sharded).
+struct ShardState {
+    dt_comm* comm = nullptr;
+    int exchange = 0;  // 0: attention kernel stores into the owners' buffers (IPC), 1: NCCL all-to-all
+    int h0 = 0, heads = 16;
+    // exchange 0: two receive buffers [G, M/G, w] bf16 (one per step parity) and every rank's
+    // mapping of them; rebuilt when M changes
+    long long recv_tokens = 0;
+    void* recv[2] = {nullptr, nullptr};
+    void* peers[2][8] = {};
+    bool opened[2][8] = {};
+    float* barrier = nullptr;  // one float all-reduced after the stores
+    int step = 0;
+};
 }  // namespace
 
 // ===========================================================================
@@ -585,6 +754,7 @@ struct dt_attn {
     size_t bws_bytes = 0;
     int last_B = 0, last_T = 0;  // shape of the last forward, whose activations the workspace holds
     bool last_varlen = false;
+    ShardState* shard = nullptr;  // head-sharded handle (dt_attn_create_sharded)
 };
 
 extern "C" {
@@ -1216,11 +1386,373 @@ int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_a
     return dt_attn_create(&w, device, out);
 }
 
+// ---- head-sharded attention layer (several GPUs) ---------------------------
+
+int dt_comm_unique_id(void* id_out) {
+    t_last_error.clear();
+    if (!id_out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    NcclApi* n;
+    DT_TRY(need_nccl(&n));
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    ncclUniqueId id;
+    const ncclResult_t r = n->GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(DT_ERR_NCCL, "ncclGetUniqueId: %s", n->GetErrorString(r));
+    std::memcpy(id_out, &id, sizeof(id));
+    return DT_OK;
+}
+
+int dt_comm_create(const void* id, int world, int rank, int device, int timeout_ms, dt_comm** out) {
+    t_last_error.clear();
+    if (!id || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (world < 1 || world > 8 || rank < 0 || rank >= world)
+        return fail(DT_ERR_INVALID_ARGUMENT, "need 1 <= world <= 8 and 0 <= rank < world (world=%d rank=%d)", world,
+                    rank);
+    if (timeout_ms <= 0) return fail(DT_ERR_INVALID_ARGUMENT, "timeout_ms must be positive");
+    NcclApi* n;
+    DT_TRY(need_nccl(&n));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    dt_comm* c = new dt_comm();
+    c->world = world;
+    c->rank = rank;
+    c->device = device;
+    c->timeout_ms = timeout_ms;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = n->CommInitRankConfig(&c->comm, world, uid, rank, &cfg);
+    const int st = nccl_done(c, r, "ncclCommInitRankConfig");
+    if (st != DT_OK) {
+        const std::string msg = t_last_error;
+        if (c->comm) n->CommAbort(c->comm);
+        delete c;
+        t_last_error = msg;
+        return st;
+    }
+    *out = c;
+    return DT_OK;
+}
+
+int dt_comm_abort(dt_comm* c) {
+    t_last_error.clear();
+    if (!c) return DT_OK;
+    if (c->comm) {
+        NcclApi* n;
+        DT_TRY(need_nccl(&n));
+        n->CommAbort(c->comm);
+        c->comm = nullptr;
+    }
+    return DT_OK;
+}
+
+int dt_comm_destroy(dt_comm* c) {
+    t_last_error.clear();
+    if (!c) return DT_OK;
+    int st = DT_OK;
+    if (c->comm) {
+        NcclApi* n;
+        DT_TRY(need_nccl(&n));
+        DeviceGuard dg;
+        DT_TRY(dg.enter(c->device));
+        st = nccl_done(c, n->CommDestroy(c->comm), "ncclCommDestroy");
+        c->comm = nullptr;
+    }
+    delete c;
+    return st;
+}
+
+int dt_qk_sumsq(const float* q, const float* k, long long ld, int width, long long M, float* ss, void* stream) {
+    t_last_error.clear();
+    if (M < 0 || width <= 0 || (width % 4) != 0 || ld < width || (ld % 4) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "need M >= 0, width a positive multiple of 4, ld >= width, ld %% 4 == 0");
+    if (M == 0) return DT_OK;
+    if (!q || !k || !ss || !aligned16(q) || !aligned16(k) || ((uintptr_t)ss & 7u))
+        return fail(DT_ERR_INVALID_ARGUMENT, "q, k 16-byte aligned and ss 8-byte aligned, non-null");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    return launch_sumsq(q, k, ld, width, M, ss, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dt_qk_norm_rope_shard(const float* q, const float* k, const float* v, long long ld_in, const float* ss,
+                          const float* q_gain, const float* k_gain, int heads, void* q_out, void* k_out, void* v_out,
+                          int B, int T, float eps, float rope_theta, void* stream) {
+    t_last_error.clear();
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    if (T > kMaxSeqLen) return fail(DT_ERR_INVALID_ARGUMENT, "T=%d exceeds max_seq_len %d", T, kMaxSeqLen);
+    if (heads != 1 && heads != 2 && heads != 4 && heads != 8 && heads != 16)
+        return fail(DT_ERR_INVALID_ARGUMENT, "heads must be 1, 2, 4, 8 or 16");
+    if ((long long)B * T == 0) return DT_OK;
+    if (ld_in < heads * 128 || (ld_in % 4) != 0)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ld_in must be >= heads*128 and a multiple of 4");
+    const void* ptrs[] = {q, k, v, q_gain, k_gain, q_out, k_out, v_out};
+    for (const void* ptr : ptrs)
+        if (!ptr || !aligned16(ptr)) return fail(DT_ERR_INVALID_ARGUMENT, "pointers must be non-null and 16-byte aligned");
+    if (!ss || ((uintptr_t)ss & 7u)) return fail(DT_ERR_INVALID_ARGUMENT, "ss must be non-null and 8-byte aligned");
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    const float *st, *ct;
+    DT_TRY(ensure_rope(dev, rope_theta, &st, &ct));
+    return launch_prologue_shard(q, k, v, ld_in, ss, q_gain, k_gain, heads, st, ct, q_out, k_out, v_out, B, T, eps,
+                                 reinterpret_cast<cudaStream_t>(stream));
+}
+
+static void shard_release(dt_attn* a) {
+    ShardState* sh = a->shard;
+    if (!sh) return;
+    for (int b = 0; b < 2; ++b)
+        for (int r = 0; r < 8; ++r)
+            if (sh->opened[b][r]) cudaIpcCloseMemHandle(sh->peers[b][r]);
+    for (int b = 0; b < 2; ++b) cudaFree(sh->recv[b]);
+    cudaFree(sh->barrier);
+    delete sh;
+    a->shard = nullptr;
+}
+
+// Receive buffers of the in-kernel exchange for M tokens, and every rank's
+// mapping of every rank's buffers (handles all-gathered over NCCL).  Collective.
+static int shard_setup_exchange(dt_attn* a, long long M, cudaStream_t st) {
+    ShardState* sh = a->shard;
+    dt_comm* c = sh->comm;
+    if (sh->recv_tokens == M) return DT_OK;
+    NcclApi* n;
+    DT_TRY(need_nccl(&n));
+    DT_CUDA(cudaStreamSynchronize(st));
+    for (int b = 0; b < 2; ++b)
+        for (int r = 0; r < 8; ++r)
+            if (sh->opened[b][r]) {
+                DT_CUDA(cudaIpcCloseMemHandle(sh->peers[b][r]));
+                sh->opened[b][r] = false;
+            }
+    for (int b = 0; b < 2; ++b) {
+        DT_CUDA(cudaFree(sh->recv[b]));
+        sh->recv[b] = nullptr;
+    }
+    sh->recv_tokens = 0;
+    const size_t bytes = align256((size_t)M * sh->heads * 128 * 2);
+    for (int b = 0; b < 2; ++b) DT_CUDA(cudaMalloc(&sh->recv[b], bytes));
+    const int G = c->world;
+    // my two handles -> device -> all-gather -> host
+    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    std::vector<uint8_t> mine(2 * kH), all((size_t)G * 2 * kH);
+    for (int b = 0; b < 2; ++b) {
+        cudaIpcMemHandle_t h;
+        DT_CUDA(cudaIpcGetMemHandle(&h, sh->recv[b]));
+        std::memcpy(mine.data() + b * kH, &h, kH);
+    }
+    uint8_t* dbuf = nullptr;
+    DT_CUDA(cudaMalloc(&dbuf, (size_t)(G + 1) * 2 * kH));
+    int rc = DT_OK;
+    if (cudaMemcpy(dbuf, mine.data(), 2 * kH, cudaMemcpyHostToDevice) != cudaSuccess) rc = DT_ERR_CUDA;
+    if (rc == DT_OK)
+        rc = nccl_done(c, n->AllGather(dbuf, dbuf + 2 * kH, 2 * kH, ncclUint8, c->comm, st), "ncclAllGather(handles)");
+    if (rc == DT_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = DT_ERR_CUDA;
+    if (rc == DT_OK && cudaMemcpy(all.data(), dbuf + 2 * kH, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = DT_ERR_CUDA;
+    cudaFree(dbuf);
+    if (rc == DT_ERR_CUDA) return fail(DT_ERR_CUDA, "exchanging the receive-buffer handles failed");
+    if (rc != DT_OK) return rc;
+    for (int b = 0; b < 2; ++b)
+        for (int r = 0; r < G; ++r) {
+            if (r == c->rank) {
+                sh->peers[b][r] = sh->recv[b];
+                continue;
+            }
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, all.data() + ((size_t)r * 2 + b) * kH, kH);
+            DT_CUDA(cudaIpcOpenMemHandle(&sh->peers[b][r], h, cudaIpcMemLazyEnablePeerAccess));
+            sh->opened[b][r] = true;
+        }
+    sh->recv_tokens = M;
+    return DT_OK;
+}
+
+int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange, dt_attn** out) {
+    t_last_error.clear();
+    if (!w || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    *out = nullptr;
+    DT_TRY(comm_ok(comm));
+    if (exchange != 0 && exchange != 1) return fail(DT_ERR_INVALID_ARGUMENT, "exchange must be 0 (in-kernel) or 1 (NCCL)");
+    if (!w->q_proj || !w->k_proj || !w->v_proj || !w->o_proj || !w->q_norm || !w->k_norm)
+        return fail(DT_ERR_INVALID_ARGUMENT, "null weight pointer");
+    if (w->d_model != 2048 || w->n_heads != 16)
+        return fail(DT_ERR_UNSUPPORTED, "need d_model 2048 and 16 heads of 128 (got d_model=%d n_heads=%d)",
+                    w->d_model, w->n_heads);
+    const int G = comm->world;
+    if (16 % G != 0) return fail(DT_ERR_UNSUPPORTED, "16 heads do not split over %d ranks", G);
+    DeviceGuard dg;
+    DT_TRY(dg.enter(comm->device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    dt_attn* a = new dt_attn();
+    a->device = comm->device;
+    a->d_model = 2048;
+    a->n_heads = 16;
+    a->eps = w->eps;
+    a->theta = w->rope_theta;
+    a->shard = new ShardState();
+    ShardState* sh = a->shard;
+    sh->comm = comm;
+    sh->exchange = exchange;
+    sh->heads = 16 / G;
+    sh->h0 = comm->rank * sh->heads;
+    const size_t d = 2048, wcols = (size_t)sh->heads * 128, dd = d * d;
+    auto cleanup = [&](int code) {
+        const std::string msg = t_last_error;
+        dt_attn_destroy(a);
+        t_last_error = msg;
+        return code;
+    };
+    // [Wq_r; Wk_r; Wv_r]: this rank's head rows of each projection, then all of Wo
+    float* stage = nullptr;
+    if (cudaMalloc(&stage, 3 * wcols * d * 4) != cudaSuccess || cudaMalloc(&a->wqkv, 3 * wcols * d * 2) != cudaSuccess ||
+        cudaMalloc(&a->wo, dd * 2) != cudaSuccess || cudaMalloc(&a->qg, d * 4) != cudaSuccess ||
+        cudaMalloc(&a->kg, d * 4) != cudaSuccess || cudaMalloc(&sh->barrier, 256) != cudaSuccess) {
+        cudaFree(stage);
+        return cleanup(fail(DT_ERR_OUT_OF_MEMORY, "cudaMalloc failed for the sharded layer's weights"));
+    }
+    const float* src[3] = {w->q_proj, w->k_proj, w->v_proj};
+    int rc = DT_OK;
+    for (int i = 0; i < 3 && rc == DT_OK; ++i)
+        if (cudaMemcpy(stage + i * wcols * d, src[i] + (size_t)sh->h0 * 128 * d, wcols * d * 4,
+                       cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = fail(DT_ERR_CUDA, "weight upload failed");
+    if (rc == DT_OK) rc = launch_cast(stage, a->wqkv, (long long)(3 * wcols * d), nullptr);
+    if (rc == DT_OK && cudaDeviceSynchronize() != cudaSuccess) rc = fail(DT_ERR_CUDA, "weight cast failed");
+    if (rc == DT_OK && cudaMemcpy(stage, w->o_proj, dd * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = fail(DT_ERR_CUDA, "weight upload failed");
+    if (rc == DT_OK) rc = launch_cast(stage, a->wo, (long long)dd, nullptr);
+    if (rc == DT_OK && cudaDeviceSynchronize() != cudaSuccess) rc = fail(DT_ERR_CUDA, "weight cast failed");
+    cudaFree(stage);
+    if (rc == DT_OK && (cudaMemcpy(a->qg, w->q_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                        cudaMemcpy(a->kg, w->k_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                        cudaMemset(sh->barrier, 0, 256) != cudaSuccess))
+        rc = fail(DT_ERR_CUDA, "gain upload failed");
+    if (rc == DT_OK) {
+        const float *st, *ct;
+        rc = ensure_rope(dev, a->theta, &st, &ct);
+    }
+    if (rc != DT_OK) return cleanup(rc);
+    *out = a;
+    return DT_OK;
+}
+
+// Workspace of a sharded forward for M tokens (w = this rank's columns):
+// x bf16 [M, 2048] | [q|k|v] fp32 [M, 3w] | sums of squares [M, 2] fp32 |
+// q, k, v bf16 [M, w] | exchange 1: local output and receive buffer bf16 [M, w] each
+static size_t shard_ws_bytes(long long M, int w) {
+    return align256(M * 2048 * 2) + align256(M * 3 * w * 4) + align256(M * 8) + 3 * align256(M * w * 2) +
+           2 * align256(M * w * 2);
+}
+
+int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y, void* stream) {
+    t_last_error.clear();
+    if (!a || !a->shard) return fail(DT_ERR_INVALID_ARGUMENT, "not a sharded handle (dt_attn_create_sharded)");
+    ShardState* sh = a->shard;
+    dt_comm* c = sh->comm;
+    DT_TRY(comm_ok(c));
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    if (T > kMaxSeqLen) return fail(DT_ERR_INVALID_ARGUMENT, "T=%d exceeds max_seq_len %d", T, kMaxSeqLen);
+    const long long M = (long long)B * T;
+    const int G = c->world;
+    if (M % G != 0) return fail(DT_ERR_INVALID_ARGUMENT, "B*T = %lld is not divisible by %d ranks", M, G);
+    if (M == 0) return DT_OK;
+    if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(DT_ERR_INVALID_ARGUMENT, "x/y must be 16-byte aligned");
+    NcclApi* n;
+    DT_TRY(need_nccl(&n));
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int w = sh->heads * 128;
+    const long long tpr = M / G;
+    const size_t need = shard_ws_bytes(M, w);
+    if (a->ws_bytes < need) {
+        DT_CUDA(cudaStreamSynchronize(st));
+        if (a->ws) DT_CUDA(cudaFree(a->ws));
+        a->ws = nullptr;
+        a->ws_bytes = 0;
+        DT_CUDA(cudaMalloc(&a->ws, need));
+        a->ws_bytes = need;
+    }
+    if (sh->exchange == 0) DT_TRY(shard_setup_exchange(a, M, st));
+    uint8_t* p = reinterpret_cast<uint8_t*>(a->ws);
+    void* xb = p;
+    p += align256(M * 2048 * 2);
+    float* qkv = reinterpret_cast<float*>(p);
+    p += align256(M * 3 * w * 4);
+    float* ss = reinterpret_cast<float*>(p);
+    p += align256(M * 8);
+    void* qb = p;
+    void* kb = p + align256(M * w * 2);
+    void* vb = p + 2 * align256(M * w * 2);
+    p += 3 * align256(M * w * 2);
+    void* o_local = p;
+    void* recv_nccl = p + align256(M * w * 2);
+    const float *sin_t, *cos_t;
+    DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
+    DT_TRY(launch_cast(x, xb, M * 2048, st));
+    // [q|k|v]_r = x [Wq_r; Wk_r; Wv_r]^T (padding-only tiles skipped, as in the one-GPU layer)
+    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * w, 2048, 3 * w, st, 1, dt::gemm::kStore, seq_lens, T, 0));
+    // QK-RMSNorm over all 2048 columns: this rank's partial sums, summed over the ranks
+    DT_TRY(launch_sumsq(qkv, qkv + w, 3 * w, w, M, ss, st));
+    DT_TRY(nccl_done(c, n->AllReduce(ss, ss, (size_t)(2 * M), ncclFloat32, ncclSum, c->comm, st),
+                     "ncclAllReduce(sums of squares)"));
+    DT_TRY(launch_prologue_shard(qkv, qkv + w, qkv + 2 * w, 3 * w, ss, a->qg + sh->h0 * 128, a->kg + sh->h0 * 128,
+                                 sh->heads, sin_t, cos_t, qb, kb, vb, B, T, a->eps, st));
+    const float scale = 1.0f / std::sqrt(128.0f);
+    const void* a_op;
+    if (G == 1) {
+        DT_TRY(launch_flash(qb, kb, vb, o_local, 1, w, nullptr, nullptr, seq_lens, B, T, sh->heads, scale, 1, st));
+        a_op = o_local;
+    } else if (sh->exchange == 0) {
+        // attention stores each row into its owner's buffer; a one-float all-reduce after
+        // the system fence orders every rank's stores before the owners' projections
+        const int buf = sh->step & 1;
+        sh->step++;
+        Scatter sc;
+        sc.ranks = G;
+        sc.plane = c->rank;
+        sc.tokens_per_rank = tpr;
+        sc.dst = sh->peers[buf];
+        DT_TRY(launch_flash(qb, kb, vb, nullptr, 1, w, nullptr, nullptr, seq_lens, B, T, sh->heads, scale, 1, st, sc));
+        dt::elem::system_fence_kernel<<<1, 32, 0, st>>>();
+        DT_CUDA(cudaGetLastError());
+        DT_TRY(nccl_done(c, n->AllReduce(sh->barrier, sh->barrier, 1, ncclFloat32, ncclSum, c->comm, st),
+                         "ncclAllReduce(barrier)"));
+        a_op = sh->recv[buf];
+    } else {
+        // local [M, w] token-major = [G, tpr, w]: slice g goes to rank g, plane g of mine comes from rank g
+        DT_TRY(launch_flash(qb, kb, vb, o_local, 1, w, nullptr, nullptr, seq_lens, B, T, sh->heads, scale, 1, st));
+        const size_t cnt = (size_t)tpr * w * 2;  // bytes per slice
+        DT_TRY(nccl_done(c, n->GroupStart(), "ncclGroupStart"));
+        int rc = DT_OK;
+        for (int r = 0; r < G && rc == DT_OK; ++r) {
+            rc = nccl_done(c, n->Send(static_cast<uint8_t*>(o_local) + r * cnt, cnt, ncclUint8, r, c->comm, st),
+                           "ncclSend");
+            if (rc == DT_OK)
+                rc = nccl_done(c, n->Recv(static_cast<uint8_t*>(recv_nccl) + r * cnt, cnt, ncclUint8, r, c->comm, st),
+                               "ncclRecv");
+        }
+        const int rc2 = nccl_done(c, n->GroupEnd(), "ncclGroupEnd");
+        if (rc != DT_OK) return rc;
+        DT_TRY(rc2);
+        a_op = recv_nccl;
+    }
+    // y_r = A_r Wo^T over this rank's token slice; A_r is planar over the G source ranks
+    return launch_gemm(a_op, a->wo, y, 0, (int)tpr, 2048, 2048, 2048, st, G);
+}
+
 int dt_attn_destroy(dt_attn* a) {
     if (!a) return DT_OK;
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(a->device);
+    shard_release(a);
     cudaFree(a->wqkv);
     cudaFree(a->wo);
     cudaFree(a->qg);
@@ -1290,6 +1822,7 @@ static int attn_workspace(dt_attn* a, long long M, uint8_t** ws) {
 int dt_attn_forward(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y, void* stream) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
     if (T > kMaxSeqLen) return fail(DT_ERR_INVALID_ARGUMENT, "T=%d exceeds max_seq_len %d", T, kMaxSeqLen);
     const long long M = (long long)B * T;
@@ -1314,6 +1847,7 @@ int dt_attn_forward(dt_attn* a, const float* x, int B, int T, const int* seq_len
 int dt_attn_forward_host(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
     const long long M = (long long)B * T;
     if (M == 0) return DT_OK;
@@ -1367,6 +1901,7 @@ static int attn_grads(dt_attn* a) {
 int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void* stream) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     if (B != a->last_B || T != a->last_T || (long long)B * T == 0)
         return fail(DT_ERR_INVALID_ARGUMENT, "backward needs the shape of the last forward (B=%d T=%d), got B=%d T=%d",
                     a->last_B, a->last_T, B, T);
@@ -1456,6 +1991,7 @@ int dt_attn_backward(dt_attn* a, const float* dy, int B, int T, float* dx, void*
 int dt_attn_backward_host(dt_attn* a, const float* dy, int B, int T, float* dx) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     if (!dy || !dx) return fail(DT_ERR_INVALID_ARGUMENT, "null dy/dx");
     const long long M = (long long)B * T;
     if (M <= 0 || B != a->last_B || T != a->last_T)
@@ -1486,6 +2022,7 @@ int dt_attn_backward_host(dt_attn* a, const float* dy, int B, int T, float* dx) 
 int dt_attn_step(dt_attn* a, float lr, void* stream) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     DeviceGuard dg;
     DT_TRY(dg.enter(a->device));
     DT_TRY(attn_grads(a));
@@ -1502,6 +2039,7 @@ int dt_attn_step(dt_attn* a, float lr, void* stream) {
 int dt_attn_zero_grad(dt_attn* a, void* stream) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     DeviceGuard dg;
     DT_TRY(dg.enter(a->device));
     if (!a->grad) return DT_OK;
@@ -1514,6 +2052,7 @@ int dt_attn_get_params_host(dt_attn* a, float* q_proj, float* k_proj, float* v_p
                             float* k_norm, int gradients) {
     t_last_error.clear();
     if (!a) return fail(DT_ERR_INVALID_ARGUMENT, "null handle");
+    if (a->shard) return fail(DT_ERR_UNSUPPORTED, "head-sharded handle: use dt_attn_forward_sharded");
     DeviceGuard dg;
     DT_TRY(dg.enter(a->device));
     DT_CUDA(cudaDeviceSynchronize());

@@ -153,6 +153,112 @@ qk_norm_rope_kernel(const PrologueParams p) {
     *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) = vw;
 }
 
+// ---------------------------------------------------------------------------
+// Head-sharded prologue (heads split over ranks, column-parallel QKV).  The
+// QK-RMSNorm sums squares over all 2048 columns of a token, i.e. over every
+// rank's heads (RMSNorm.cpp:17, applied at OlmoAttention.cpp:70,76), so it runs
+// in two steps around one all-reduce of 2 floats per token:
+//   qk_sumsq_kernel            ss[row] = {sum q^2, sum k^2} over this rank's
+//                              `width` = heads * 128 columns;
+//   (all-reduce ss over the ranks: the full-row sums)
+//   qk_norm_rope_shard_kernel  y = x / sqrt(ss / 2048 + eps) * g, RoPE, bf16,
+//                              for this rank's heads only.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+qk_sumsq_kernel(const float* __restrict__ q, const float* __restrict__ k, long long ld, int width, long long M,
+                float2* __restrict__ ss) {
+    // one warp per token
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const float4* qr = reinterpret_cast<const float4*>(q + row * ld);
+    const float4* kr = reinterpret_cast<const float4*>(k + row * ld);
+    float sq = 0.f, sk = 0.f;
+    for (int c = lane; c < width / 4; c += 32) {
+        const float4 a = qr[c], b = kr[c];
+        sq += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+        sk += b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    if (lane == 0) ss[row] = make_float2(sq, sk);
+}
+
+struct ShardPrologueParams {
+    const float* q;       // [M, ld_in]: this rank's q columns (width = heads * 128)
+    const float* k;
+    const float* v;
+    long long ld_in;
+    const float2* ss;     // [M] full-row sums of squares {q, k}
+    const float* q_gain;  // [width]: this rank's slice of the 2048 gains
+    const float* k_gain;
+    const float* sin_t;   // [max_seq, 128]
+    const float* cos_t;
+    __nv_bfloat16* qo;    // [M, width]
+    __nv_bfloat16* ko;
+    __nv_bfloat16* vo;
+    int heads;            // 1, 2, 4, 8 or 16
+    int T;
+    long long M;
+    float eps;
+};
+
+// 16 threads per (token, head), as qk_norm_rope_kernel; a CTA of 256 threads
+// covers 16 / heads tokens.
+__global__ void __launch_bounds__(kPrologueThreads)
+qk_norm_rope_shard_kernel(const ShardPrologueParams p) {
+    const int per_tok = p.heads * 16;
+    const long long row = (long long)blockIdx.x * (kPrologueThreads / per_tok) + threadIdx.x / per_tok;
+    if (row >= p.M) return;
+    const int tid = threadIdx.x % per_tok;
+    const int h = tid >> 4;
+    const int j = tid & 15;
+    const int width = p.heads * kHeadDim;
+    const int t = static_cast<int>(row % p.T);
+    const int d_lo = h * kHeadDim + 4 * j;
+    const int d_hi = d_lo + 64;
+    const float* qr = p.q + row * p.ld_in;
+    const float* kr = p.k + row * p.ld_in;
+    const float* vr = p.v + row * p.ld_in;
+    const float4 qa = *reinterpret_cast<const float4*>(qr + d_lo);
+    const float4 qb = *reinterpret_cast<const float4*>(qr + d_hi);
+    const float4 ka = *reinterpret_cast<const float4*>(kr + d_lo);
+    const float4 kb = *reinterpret_cast<const float4*>(kr + d_hi);
+    const float4 va = *reinterpret_cast<const float4*>(vr + 8 * tid);
+    const float4 vb = *reinterpret_cast<const float4*>(vr + 8 * tid + 4);
+    const float2 s2 = p.ss[row];
+    const float rq = sqrtf(s2.x / (float)kDModel + p.eps);
+    const float rk = sqrtf(s2.y / (float)kDModel + p.eps);
+    const float* cs = p.cos_t + (long long)t * kHeadDim + 4 * j;
+    const float* sn = p.sin_t + (long long)t * kHeadDim + 4 * j;
+    const float4 c_lo = *reinterpret_cast<const float4*>(cs);
+    const float4 c_hi = *reinterpret_cast<const float4*>(cs + 64);
+    const float4 s_lo = *reinterpret_cast<const float4*>(sn);
+    const float4 s_hi = *reinterpret_cast<const float4*>(sn + 64);
+    const float4 gq_lo = *reinterpret_cast<const float4*>(p.q_gain + d_lo);
+    const float4 gq_hi = *reinterpret_cast<const float4*>(p.q_gain + d_hi);
+    const float4 gk_lo = *reinterpret_cast<const float4*>(p.k_gain + d_lo);
+    const float4 gk_hi = *reinterpret_cast<const float4*>(p.k_gain + d_hi);
+    auto rot = [&](float4 a, float4 b, float r, float4 ga, float4 gb, __nv_bfloat16* out) {
+        const float a0 = a.x / r * ga.x, a1 = a.y / r * ga.y, a2 = a.z / r * ga.z, a3 = a.w / r * ga.w;
+        const float b0 = b.x / r * gb.x, b1 = b.y / r * gb.y, b2 = b.z / r * gb.z, b3 = b.w / r * gb.w;
+        uint2 lo, hi;
+        lo.x = pack_bf16x2(a0 * c_lo.x - b0 * s_lo.x, a1 * c_lo.y - b1 * s_lo.y);
+        lo.y = pack_bf16x2(a2 * c_lo.z - b2 * s_lo.z, a3 * c_lo.w - b3 * s_lo.w);
+        hi.x = pack_bf16x2(b0 * c_hi.x + a0 * s_hi.x, b1 * c_hi.y + a1 * s_hi.y);
+        hi.y = pack_bf16x2(b2 * c_hi.z + a2 * s_hi.z, b3 * c_hi.w + a3 * s_hi.w);
+        *reinterpret_cast<uint2*>(out + row * width + d_lo) = lo;
+        *reinterpret_cast<uint2*>(out + row * width + d_hi) = hi;
+    };
+    rot(qa, qb, rq, gq_lo, gq_hi, p.qo);
+    rot(ka, kb, rk, gk_lo, gk_hi, p.ko);
+    *reinterpret_cast<uint4*>(p.vo + row * width + 8 * tid) =
+        make_uint4(pack_bf16x2(va.x, va.y), pack_bf16x2(va.z, va.w), pack_bf16x2(vb.x, vb.y), pack_bf16x2(vb.z, vb.w));
+}
+
 }  // namespace elem
 }  // namespace dt
 

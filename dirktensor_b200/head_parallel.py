@@ -222,3 +222,201 @@ class HeadParallelAttention:
         return self.project(a, self.world, out)
 
     __call__ = forward
+
+
+# ---------------------------------------------------------------------------
+# The full attention layer, head-parallel
+# ---------------------------------------------------------------------------
+class HeadParallelAttentionLayer(HeadParallelAttention):
+    """OlmoAttention::forward (OlmoAttention.cpp:56-108) with the heads sharded
+    over the process group, orchestrated with torch.distributed:
+
+      [q|k|v]_r = x [Wq_r; Wk_r; Wv_r]^T   column-parallel: rank r's head rows
+      s_r = per-token sums of squares of q_r and k_r, all-reduced: QK-RMSNorm
+            normalises over all 2048 columns (RMSNorm.cpp:17), i.e. over every
+            rank's heads, so 2 floats per token cross the ranks
+      q_r, k_r = RoPE(q_r / rms * g_r); v_r     this rank's heads only
+      attention + token-sliced exchange + O projection of HeadParallelAttention.
+
+    ``forward(x)`` takes the full input [B, T, 2048] float32 on every rank and
+    returns this rank's token slice of y ([B*T/G, 2048]).  The same
+    orchestration for C/C++ callers is ShardedOlmoAttention (the C ABI's
+    dt_attn_create_sharded / dt_attn_forward_sharded, on a communicator of its
+    own).  The compute steps are methods so that host tests can replace them.
+    """
+
+    def __init__(self, wq, wk, wv, wo, q_norm, k_norm, group: Optional[dist.ProcessGroup] = None,
+                 exchange: str = "fused", eps: float = 1e-6, theta: float = 500000.0):
+        super().__init__(wo, n_heads=16, head_dim=128, group=group, exchange=exchange)
+        rows = slice(self.h0 * self.head_dim, self.h1 * self.head_dim)
+        self.width = (self.h1 - self.h0) * self.head_dim
+        self.wqkv = self._prepare_wqkv(torch.cat([wq[rows], wk[rows], wv[rows]]).contiguous())
+        self.q_gain = q_norm[rows].contiguous()
+        self.k_gain = k_norm[rows].contiguous()
+        self.eps = eps
+        self.theta = theta
+
+    # ---- compute steps (CUDA library) ------------------------------------
+    def _prepare_wqkv(self, w):
+        return _attn.cast_bf16(w)
+
+    def project_qkv(self, x2d):
+        """[M, 2048] float32 -> [M, 3w] float32 (this rank's q, k, v columns)."""
+        return _attn.gemm_bf16_tn(_attn.cast_bf16(x2d.contiguous()), self.wqkv)
+
+    def sums_of_squares(self, qkv):
+        """Per-token {sum q^2, sum k^2} over this rank's columns: [M, 2] float32."""
+        M = qkv.shape[0]
+        ss = torch.empty((M, 2), dtype=torch.float32, device=qkv.device)
+        w = self.width
+        check(lib().dt_qk_sumsq(qkv.data_ptr(), qkv[:, w:].data_ptr(), qkv.stride(0), w, M, ss.data_ptr(),
+                                torch.cuda.current_stream(qkv.device).cuda_stream))
+        return ss
+
+    def norm_rope(self, qkv, ss, B: int, T: int):
+        """q, k normalised with the full-row sums and RoPE'd, v copied: bf16 [B, T, Hl, D] each."""
+        M, w = qkv.shape[0], self.width
+        Hl = self.h1 - self.h0
+        outs = [torch.empty((B, T, Hl, self.head_dim), dtype=torch.bfloat16, device=qkv.device) for _ in range(3)]
+        check(lib().dt_qk_norm_rope_shard(qkv.data_ptr(), qkv[:, w:].data_ptr(), qkv[:, 2 * w:].data_ptr(),
+                                          qkv.stride(0), ss.data_ptr(), self.q_gain.data_ptr(),
+                                          self.k_gain.data_ptr(), Hl, outs[0].data_ptr(), outs[1].data_ptr(),
+                                          outs[2].data_ptr(), B, T, float(self.eps), float(self.theta),
+                                          torch.cuda.current_stream(qkv.device).cuda_stream))
+        return tuple(outs)
+
+    def attention_bf16(self, qb, kb, vb, seq_lens):
+        """Attention on this rank's heads (bf16 operands) -> the A operand of the
+        O projection: [M, w] (one rank) or [G, M/G, w] (after the exchange)."""
+        B, T, Hl, D = qb.shape
+        M = B * T
+        G = self.world
+        scale = 1.0 / float(D) ** 0.5
+        lens = None if seq_lens is None else torch.as_tensor(seq_lens, dtype=torch.int32,
+                                                             device=qb.device).contiguous()
+        stream = torch.cuda.current_stream(qb.device).cuda_stream
+        if G > 1 and self.exchange_mode == "fused":
+            if lens is not None:
+                raise ValueError("the in-kernel exchange of this Python layer takes no seq_lens; "
+                                 "use exchange='nccl' or ShardedOlmoAttention")
+            self._setup_fused(M, Hl * D, qb.device)
+            buf = self._step & 1
+            self._step += 1
+            check(lib().dt_flash_fwd_bf16_exchange(qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), self._fused[2][buf],
+                                                   G, self.rank, M // G, None, None, B, T, Hl, D, scale, 1, stream))
+            dist.all_reduce(self._barrier, group=self.group)
+            return self._fused[1][buf]
+        out = self._buf("o_local", (M, Hl * D), torch.bfloat16, qb.device)
+        check(lib().dt_flash_fwd_bf16(qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), out.data_ptr(), 1, Hl * D, None,
+                                      None, None if lens is None else lens.data_ptr(), B, T, Hl, D, scale, 1,
+                                      stream))
+        return self.exchange(out)
+
+    def forward(self, x, seq_lens=None, out: Optional[torch.Tensor] = None):  # type: ignore[override]
+        B, T, d = x.shape
+        M = B * T
+        token_range(self.rank, self.world, M)  # validates divisibility
+        qkv = self.project_qkv(x.reshape(M, d))
+        ss = self.sums_of_squares(qkv)
+        if self.world > 1:
+            dist.all_reduce(ss, group=self.group)
+        qb, kb, vb = self.norm_rope(qkv, ss, B, T)
+        a = self.attention_bf16(qb, kb, vb, seq_lens)
+        return self.project(a, self.world, out)
+
+    __call__ = forward
+
+
+class Communicator:
+    """An NCCL communicator of the CUDA library (dt_comm) for this rank.
+
+    ``Communicator.from_process_group()`` makes rank 0's 128-byte NCCL id
+    (dt_comm_unique_id), hands it to the other ranks through torch.distributed
+    (any backend), and creates the communicator on the current CUDA device with
+    a set-up timeout (a rank that never joins makes the others fail with
+    DT_ERR_TIMEOUT instead of hanging)."""
+
+    def __init__(self, world: int, rank: int, uid: bytes, device: int, timeout_ms: int = 60000):
+        self._c = ctypes.c_void_p()
+        self.world, self.rank, self.device = world, rank, device
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+        check(lib().dt_comm_create(buf, world, rank, device, int(timeout_ms), ctypes.byref(self._c)))
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (ctypes.c_uint8 * 128)()
+        check(lib().dt_comm_unique_id(buf))
+        return bytes(buf)
+
+    @classmethod
+    def from_process_group(cls, group: Optional[dist.ProcessGroup] = None, device: Optional[int] = None,
+                           timeout_ms: int = 60000) -> "Communicator":
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        dev = torch.cuda.current_device() if device is None else device
+        uid = cls.unique_id() if rank == 0 else bytes(128)
+        if world > 1:
+            backend = dist.get_backend(group)
+            t = torch.tensor(list(uid), dtype=torch.uint8,
+                             device=torch.device("cuda", dev) if backend == "nccl" else "cpu")
+            dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+            uid = bytes(t.cpu().tolist())
+        return cls(world, rank, uid, dev, timeout_ms)
+
+    @property
+    def handle(self):
+        return self._c
+
+    def abort(self):
+        if self._c:
+            check(lib().dt_comm_abort(self._c))
+
+    def close(self):
+        if self._c:
+            check(lib().dt_comm_destroy(self._c))
+            self._c = ctypes.c_void_p()
+
+
+class ShardedOlmoAttention:
+    """The head-parallel attention layer of the C ABI (dt_attn_create_sharded,
+    dt_attn_forward_sharded): the same steps as HeadParallelAttentionLayer, with
+    the collectives issued by the library on its own NCCL communicator, so that
+    C and C++ callers need no Python.  ``forward(x)`` takes the full input
+    [B, T, 2048] float32 on every rank and returns this rank's token slice of y
+    ([B*T/G, 2048]); exchange "fused" = in-kernel NVLink stores, "nccl" = NCCL
+    all-to-all."""
+
+    def __init__(self, wq, wk, wv, wo, q_norm, k_norm, comm: Communicator, exchange: str = "fused",
+                 eps: float = 1e-6, theta: float = 500000.0):
+        import numpy as np
+
+        if exchange not in ("fused", "nccl"):
+            raise ValueError("exchange must be 'fused' or 'nccl'")
+        arrs = [np.ascontiguousarray(a.cpu().numpy() if hasattr(a, "cpu") else a, dtype=np.float32)
+                for a in (wq, wk, wv, wo, q_norm, k_norm)]
+        w = _attn.dt_attn_weights(*(a.ctypes.data for a in arrs), 2048, 16, eps, theta)
+        self._h = ctypes.c_void_p()
+        self.comm = comm
+        check(lib().dt_attn_create_sharded(ctypes.byref(w), comm.handle, 0 if exchange == "fused" else 1,
+                                           ctypes.byref(self._h)))
+
+    def forward(self, x, seq_lens=None, out: Optional[torch.Tensor] = None):
+        B, T, d = x.shape
+        G = self.comm.world
+        if (B * T) % G:
+            raise ValueError(f"B*T = {B * T} is not divisible by {G} ranks")
+        y = out if out is not None else torch.empty((B * T // G, d), dtype=torch.float32, device=x.device)
+        lens = None
+        if seq_lens is not None:
+            lens = torch.as_tensor(seq_lens, dtype=torch.int32, device=x.device).contiguous()
+        check(lib().dt_attn_forward_sharded(self._h, x.contiguous().data_ptr(), B, T,
+                                            None if lens is None else lens.data_ptr(), y.data_ptr(),
+                                            torch.cuda.current_stream(x.device).cuda_stream))
+        return y
+
+    __call__ = forward
+
+    def close(self):
+        if self._h:
+            lib().dt_attn_destroy(self._h)
+            self._h = ctypes.c_void_p()

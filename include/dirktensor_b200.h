@@ -33,7 +33,9 @@ enum dt_status {
     DT_ERR_DEVICE_TIMEOUT = 3,   /* a kernel's bounded wait expired (no hang)    */
     DT_ERR_UNSUPPORTED = 4,      /* e.g. head_dim != 128, no sm_100 device       */
     DT_ERR_OUT_OF_MEMORY = 5,
-    DT_ERR_IO = 6                /* checkpoint file missing or malformed         */
+    DT_ERR_IO = 6,               /* checkpoint file missing or malformed         */
+    DT_ERR_NCCL = 7,             /* NCCL missing, or a communicator call failed  */
+    DT_ERR_TIMEOUT = 8           /* a host-side wait (communicator set-up) expired */
 };
 
 /* Message for the last failing call on this thread ("" if none).
@@ -197,6 +199,51 @@ int dt_attn_get_params_host(dt_attn* attn, float* q_proj, float* k_proj, float* 
                             float* k_norm, int gradients);
 int dt_attn_destroy(dt_attn* attn);
 
+/* ---- head-parallel attention layer (several GPUs of one node) ------------
+ * The reference runs every head of a layer in one process, parallelising the
+ * attention core over batch x heads (FlashAttention.cpp:43-45).  Here the 16
+ * heads are split over G = 1, 2, 4 or 8 GPUs, one process (or thread) per GPU:
+ * rank r owns heads [r*16/G, (r+1)*16/G).  Per forward, on every rank:
+ *   [q|k|v]_r = x [Wq_r; Wk_r; Wv_r]^T        (rows of this rank's heads only)
+ *   s_r = per-token sums of squares of q_r, k_r; all-reduce over the ranks
+ *         (QK-RMSNorm normalises over all 2048 columns, RMSNorm.cpp:17, so it
+ *         needs every rank's heads: 2 floats per token cross NVLink)
+ *   q_r, k_r = RoPE(q_r / rms * g), v_r          (this rank's heads)
+ *   attention on this rank's heads; each output row is stored into the rank
+ *         that owns its token (token slice [r*M/G, (r+1)*M/G), M = B*T) --
+ *         by the attention kernel itself over NVLink (exchange 0) or by an
+ *         NCCL all-to-all (exchange 1)
+ *   y_r = A_r Wo^T for this rank's token slice, A_r = all heads of its tokens.
+ * x is the full [B, T, d_model] input on every rank; y is this rank's token
+ * slice [B*T/G, d_model] (rows r*M/G ... of the flattened [B*T, d_model]).
+ *
+ * Communicator: one NCCL communicator per rank, created from a 128-byte id
+ * that rank 0 makes with dt_comm_unique_id and hands to the other ranks
+ * (files, sockets, MPI -- the library does not care).  dt_comm_create
+ * initialises it without blocking and gives up after timeout_ms (aborting the
+ * half-built communicator) with DT_ERR_TIMEOUT, so a rank that never joins
+ * cannot hang the others' set-up.  NCCL is loaded at run time (libnccl.so.2);
+ * without it these calls return DT_ERR_NCCL and nothing else is affected. */
+typedef struct dt_comm dt_comm;
+int dt_comm_unique_id(void* id_out /* 128 bytes */);
+int dt_comm_create(const void* id, int world, int rank, int device, int timeout_ms, dt_comm** out);
+/* Aborts the communicator's outstanding work (for a caller's watchdog). */
+int dt_comm_abort(dt_comm* comm);
+int dt_comm_destroy(dt_comm* comm);
+/* Uploads this rank's share of the layer (its heads' rows of Wq, Wk, Wv, all
+ * of Wo and of the norm gains) to the communicator's device.  Every rank
+ * passes the same full weights.  exchange: 0 = attention kernel stores into
+ * the owners' buffers over NVLink (CUDA IPC; all ranks on one node), 1 = NCCL
+ * all-to-all.  Collective: every rank calls it. */
+int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange, dt_attn** out);
+/* Collective forward (every rank, same B, T, seq_lens).  x: [B, T, d_model]
+ * fp32 device array (the full input), y: [B*T/G, d_model] fp32 device array
+ * (this rank's token slice); B*T must be divisible by G.  seq_lens: device
+ * int[B] or NULL (right padding: rows t >= seq_lens[b] of y are zero).
+ * Enqueued on `stream`; the NCCL calls use the same stream.  The handle is
+ * destroyed with dt_attn_destroy; the communicator outlives it. */
+int dt_attn_forward_sharded(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y, void* stream);
+
 /* ---- full model prefill (configuration 3) -------------------------------
  * Replaces OlmoModel::forward (OlmoModel.cpp:25-48) with OlmoBlock::forward
  * (OlmoBlock.cpp:13-21), OlmoMlp::forward (OlmoMlp.cpp:26-63) and
@@ -278,6 +325,17 @@ int dt_gemm_bf16_tn_planar(const void* A, int a_planes, const void* B, void* C, 
 int dt_qk_norm_rope(const float* q, const float* k, const float* v, long long ld_in, const float* q_gain,
                     const float* k_gain, void* q_out, void* k_out, void* v_out, int B, int T, float eps,
                     float rope_theta, void* stream);
+/* Head-sharded prologue, first step: ss[r] = {sum q^2, sum k^2} over the
+ * `width` columns of row r of q and k (fp32, ld elements per row; width a
+ * multiple of 4).  Summed over the ranks, these are the full-row sums. */
+int dt_qk_sumsq(const float* q, const float* k, long long ld, int width, long long M, float* ss, void* stream);
+/* Head-sharded prologue, second step, for `heads` (1, 2, 4, 8, 16) heads:
+ * q, k normalised with the full-row sums ss ([M, 2] fp32) and this rank's
+ * slice of the gains (q_gain, k_gain: [heads*128]), RoPE'd; v copied; outputs
+ * bf16 [M, heads*128] with M = B*T. */
+int dt_qk_norm_rope_shard(const float* q, const float* k, const float* v, long long ld_in, const float* ss,
+                          const float* q_gain, const float* k_gain, int heads, void* q_out, void* k_out, void* v_out,
+                          int B, int T, float eps, float rope_theta, void* stream);
 /* Host copy of the RoPE tables the device uses ([max_seq, head_dim] each),
  * computed like compute_rope_buffers (OlmoAttention.cpp:18-36). */
 int dt_rope_tables(float* sin_out, float* cos_out, int max_seq, int head_dim, float theta);
