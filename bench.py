@@ -210,7 +210,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="N>1: fused flash + NVLink stores (default) or an NCCL all-to-all")
-    ap.add_argument("--case", default=None, choices=["flash_bf16", "flash_bwd", "layer", "gemm", "prologue", "flash_api"],
+    ap.add_argument("--case", default=None, choices=["flash_bf16", "flash_bwd", "layer", "gemm", "prologue", "flash_api", "step4"],
                     help="profiling case for ncu: a few launches of one stage, no timing")
     ap.add_argument("--sweep", action="store_true",
                     help="config-1 sweep (T = 64 ... 6144) and config 4: flash kernel TFLOP/s per shape")
@@ -295,6 +295,12 @@ def main():
     e2e = bench_e2e(torch, dev, hp, q, k, v, world, max(3, min(args.steps, 10)), barrier, max_over_ranks)
     e2e["value"] = flops_step / (e2e["ms_per_step"] * 1e-3) / 1e12
 
+    # ---- the other exchanges (N > 1) and the head-parallel layer ------------
+    variants = None
+    if world > 1:
+        variants = bench_exchange_variants(torch, dev, q, k, v, wo, world, args, barrier, max_over_ranks)
+    layers_sharded = bench_layers_sharded(torch, dev, world, args, barrier, max_over_ranks)
+
     # ---- config 1 at T=4096 (north-star single-GPU target) ---------------
     t4096 = None
     if world == 1:
@@ -375,6 +381,8 @@ def main():
             "gpu_launches": (4 if world > 1 and args.exchange == "fused" else 3) * args.steps,
             "clocks": clocks,
             "config1_t4096": t4096,
+            "exchange_variants": variants,
+            "layers_sharded": layers_sharded,
             "layers": layers,
             "prologue": prologue,
             "model_config3": model3,
@@ -385,6 +393,82 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def bench_exchange_variants(torch, dev, q, k, v, wo, world, args, barrier, max_over_ranks):
+    """N > 1: the config-4 step with the other two exchanges -- the NCCL
+    all-to-all of token slices, and the replicated form the task statement
+    names (all-gather of every rank's per-head outputs, then every rank
+    projects all B*T tokens; its O-projection FLOPs are counted once)."""
+    from dirktensor_b200.head_parallel import HeadParallelAttention
+
+    out = {}
+    for mode in ("nccl", "allgather"):
+        hp = HeadParallelAttention(wo, n_heads=H, head_dim=D, exchange=mode)
+        for _ in range(args.warmup):
+            hp.forward(q, k, v, SCALE, True)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            hp.forward(q, k, v, SCALE, True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        hp.close()
+        out[mode] = {"ms_per_step": ms, "tflops": (F_ATTN + F_OPROJ) / (ms * 1e-3) / 1e12,
+                     "received_bytes_per_rank": (world - 1) * B * T * (H // world) * D * 2 // (
+                         1 if mode == "allgather" else world)}
+    return out
+
+
+def bench_layers_sharded(torch, dev, world, args, barrier, max_over_ranks):
+    """The attention layer (OlmoAttention::forward) head-parallel over the N
+    GPUs through the C ABI (dt_attn_create_sharded / dt_attn_forward_sharded on
+    the library's own NCCL communicator; in-kernel exchange): config 0 (B=1,
+    T=512) and config 2 (B=8, T_max=2048, right-padded, seeded lengths in
+    [256, 2048]).  Every rank holds the full input and returns its token slice.
+    tok/s counts valid tokens; L2 flushed before every timed forward."""
+    from dirktensor_b200.head_parallel import Communicator, ShardedOlmoAttention
+
+    rng = np.random.default_rng(0)
+    w = [(0.02 * rng.standard_normal((DM, DM), dtype=np.float32)) for _ in range(4)]
+    gains = [(1 + 0.02 * rng.standard_normal(DM, dtype=np.float32)).astype(np.float32) for _ in range(2)]
+    comm = Communicator.from_process_group(timeout_ms=120000)
+    layer = ShardedOlmoAttention(*w, *gains, comm=comm, exchange="fused")
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    out = {}
+    for name, Bl, Tl, lens in [("config0", 1, 512, None),
+                               ("config2", 8, 2048, np.random.default_rng(2).integers(256, 2049, 8))]:
+        x = torch.from_numpy(rng.standard_normal((Bl, Tl, DM), dtype=np.float32)).to(dev)
+        y = torch.empty((Bl * Tl // world, DM), dtype=torch.float32, device=dev)
+        lens_t = None if lens is None else torch.as_tensor(lens, dtype=torch.int32, device=dev)
+        valid = Bl * Tl if lens is None else int(np.sum(lens))
+        seqs = [Tl] * Bl if lens is None else [int(v) for v in lens]
+        flops = 2.0 * valid * DM * 8192 + sum(2.0 * H * L * L * D for L in seqs)
+        reps = max(3, min(args.steps, 20))
+        ts = []
+        for i in range(args.warmup + reps):
+            flush.fill_(float(i))
+            torch.cuda.synchronize()
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            layer.forward(x, seq_lens=lens_t, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(a.elapsed_time(b))
+        ms = max_over_ranks(statistics.median(ts))
+        out[name] = {"B": Bl, "T": Tl, "valid_tokens": valid, "ms": ms, "tok_s": valid / (ms * 1e-3),
+                     "tflops": flops / (ms * 1e-3) / 1e12, "gpus": world}
+    torch.cuda.synchronize()
+    barrier()
+    layer.close()
+    comm.close()
+    return out
 
 
 def bench_e2e(torch, dev, hp, q, k, v, world, steps, barrier, max_over_ranks, chunks=8):
@@ -895,6 +979,14 @@ def run_case(args):
         fwd = dt.flash_attention_forward(q, k, v, SCALE, True)
         for _ in range(3):
             dt.flash_attention_backward(do, fwd.output, fwd.softmax_m, fwd.softmax_l, q, k, v, SCALE, True)
+    elif args.case == "step4":
+        from dirktensor_b200.head_parallel import HeadParallelAttention
+
+        q, k, v = (torch.randn((B, T, H, D), generator=g, device=dev) for _ in range(3))
+        hp = HeadParallelAttention(torch.randn((DM, DM), generator=g, device=dev) * 0.02, n_heads=H, head_dim=D)
+        for _ in range(5):
+            hp.forward(q, k, v, SCALE, True)
+        hp.close()
     elif args.case == "prologue":
         qkv = torch.randn((Bc * Tc, 3 * DM), generator=g, device=dev)
         gq = torch.ones(DM, device=dev)

@@ -132,7 +132,9 @@ SIGNATURES = {
     "dt_comm_abort": (_I, [_P]),
     "dt_comm_destroy": (_I, [_P]),
     "dt_attn_create_sharded": (_I, [ctypes.POINTER(dt_attn_weights), _P, _I, ctypes.POINTER(_P)]),
-    "dt_attn_forward_sharded": (_I, [_P, _P, _I, _I, _P, _P, _P]),
+    "dt_attn_forward_sharded": (_I, [_P, _P, _I, _I, _P, _I, _P, _P]),
+    "dt_attn_forward_sharded_host": (_I, [_P, _P, _I, _I, _P, _I, _P]),
+    "dt_attn_create_sharded_from_npy": (_I, [ctypes.c_char_p, ctypes.c_uint, _P, _I, ctypes.POINTER(_P)]),
 }
 
 

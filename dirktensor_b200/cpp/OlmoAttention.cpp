@@ -1,5 +1,6 @@
 // OlmoAttention over the C ABI (dt_attn_create_from_npy, dt_attn_forward_host,
-// dt_attn_backward_host, dt_attn_step, dt_attn_zero_grad).
+// dt_attn_backward_host, dt_attn_step, dt_attn_zero_grad; head-parallel:
+// dt_attn_create_sharded_from_npy, dt_attn_forward_sharded_host).
 #include "OlmoAttention.h"
 
 #include <cstdlib>
@@ -16,23 +17,37 @@ int device_from_env() {
     return s ? std::atoi(s) : 0;
 }
 [[noreturn]] void raise(const char* what) { throw std::runtime_error(std::string(what) + ": " + dt_last_error()); }
+dt_comm* g_tp_comm = nullptr;
+int g_tp_exchange = 0;
 }  // namespace
 
+void dirktensor_b200::set_tensor_parallel(dt_comm* comm, int exchange) {
+    g_tp_comm = comm;
+    g_tp_exchange = exchange;
+}
+
 OlmoAttention::OlmoAttention(const std::string& folder, unsigned int index) {
-    if (dt_attn_create_from_npy(folder.c_str(), index, device_from_env(), &m_handle) != DT_OK)
+    if (g_tp_comm) {
+        if (dt_attn_create_sharded_from_npy(folder.c_str(), index, g_tp_comm, g_tp_exchange, &m_handle) != DT_OK)
+            raise("OlmoAttention");
+        m_sharded = true;
+    } else if (dt_attn_create_from_npy(folder.c_str(), index, device_from_env(), &m_handle) != DT_OK) {
         raise("OlmoAttention");
+    }
 }
 
 OlmoAttention::~OlmoAttention() {
     if (m_handle) dt_attn_destroy(m_handle);
 }
 
-OlmoAttention::OlmoAttention(OlmoAttention&& other) noexcept : m_handle(std::exchange(other.m_handle, nullptr)) {}
+OlmoAttention::OlmoAttention(OlmoAttention&& other) noexcept
+    : m_handle(std::exchange(other.m_handle, nullptr)), m_sharded(other.m_sharded) {}
 
 OlmoAttention& OlmoAttention::operator=(OlmoAttention&& other) noexcept {
     if (this != &other) {
         if (m_handle) dt_attn_destroy(m_handle);
         m_handle = std::exchange(other.m_handle, nullptr);
+        m_sharded = other.m_sharded;
     }
     return *this;
 }
@@ -41,9 +56,11 @@ xt::xtensor<float, 3> OlmoAttention::forward(const xt::xtensor<float, 3>& input)
     const std::size_t b = input.shape(0), t = input.shape(1), d = input.shape(2);
     if (d != d_model) throw std::invalid_argument("OlmoAttention::forward: last dimension must be d_model");
     xt::xtensor<float, 3> out = xt::empty<float>({b, t, d});
-    if (dt_attn_forward_host(m_handle, input.data(), static_cast<int>(b), static_cast<int>(t), nullptr,
-                             out.data()) != DT_OK)
-        raise("OlmoAttention::forward");
+    const int st = m_sharded ? dt_attn_forward_sharded_host(m_handle, input.data(), static_cast<int>(b),
+                                                             static_cast<int>(t), nullptr, 1, out.data())
+                             : dt_attn_forward_host(m_handle, input.data(), static_cast<int>(b), static_cast<int>(t),
+                                                    nullptr, out.data());
+    if (st != DT_OK) raise("OlmoAttention::forward");
     return out;
 }
 

@@ -10,6 +10,22 @@
 #include <xtensor/containers/xtensor.hpp>
 
 struct dt_attn;
+struct dt_comm;
+
+namespace dirktensor_b200 {
+// Head-parallel mode for this process (one process, or thread, per GPU of one
+// node; comm from dt_comm_create).  After set_tensor_parallel(comm), every
+// OlmoAttention constructed from (folder, index) holds only this rank's heads
+// of the layer (dt_attn_create_sharded_from_npy), and forward() returns the
+// whole [batch, seq, d_model] output on every rank (the ranks' token slices
+// all-gathered), so OlmoBlock and OlmoModel run head-parallel unchanged; every
+// rank must call forward with the same input.  exchange: 0 = the attention
+// kernel stores rows into their owners' buffers over NVLink, 1 = NCCL
+// all-to-all.  backward/step/zero_grad stay single-GPU and throw on a
+// head-parallel layer.  set_tensor_parallel(nullptr) returns to one GPU for
+// layers constructed afterwards; the communicator must outlive the layers.
+void set_tensor_parallel(dt_comm* comm, int exchange = 0);
+}  // namespace dirktensor_b200
 
 class OlmoAttention {
 public:
@@ -35,4 +51,5 @@ public:
 
 private:
     dt_attn* m_handle = nullptr;
+    bool m_sharded = false;
 };

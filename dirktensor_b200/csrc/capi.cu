@@ -1358,11 +1358,9 @@ static int read_npy_f32(const std::string& path, std::vector<float>& data, std::
     return DT_OK;
 }
 
-int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_attn** out) {
-    t_last_error.clear();
-    if (!folder || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+// The six weight files of attention layer `index` (OlmoAttention.cpp:39-46).
+static int read_attn_npy(const char* folder, unsigned index, std::vector<float> (&buf)[6]) {
     const char* names[6] = {"q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"};
-    std::vector<float> buf[6];
     for (int i = 0; i < 6; ++i) {
         std::vector<long long> shape;
         const std::string path = std::string(folder) + "/model.layers." + std::to_string(index) + ".self_attn." +
@@ -1372,6 +1370,14 @@ int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_a
                                 : (shape.size() == 1 && shape[0] == 2048);
         if (!ok) return fail(DT_ERR_IO, "%s: unexpected shape", path.c_str());
     }
+    return DT_OK;
+}
+
+int dt_attn_create_from_npy(const char* folder, unsigned index, int device, dt_attn** out) {
+    t_last_error.clear();
+    if (!folder || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    std::vector<float> buf[6];
+    DT_TRY(read_attn_npy(folder, index, buf));
     dt_attn_weights w;
     w.q_proj = buf[0].data();
     w.k_proj = buf[1].data();
@@ -1648,7 +1654,8 @@ static size_t shard_ws_bytes(long long M, int w) {
            2 * align256(M * w * 2);
 }
 
-int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int* seq_lens, float* y, void* stream) {
+int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int* seq_lens, int gather, float* y,
+                            void* stream) {
     t_last_error.clear();
     if (!a || !a->shard) return fail(DT_ERR_INVALID_ARGUMENT, "not a sharded handle (dt_attn_create_sharded)");
     ShardState* sh = a->shard;
@@ -1744,7 +1751,67 @@ int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int*
         a_op = recv_nccl;
     }
     // y_r = A_r Wo^T over this rank's token slice; A_r is planar over the G source ranks
-    return launch_gemm(a_op, a->wo, y, 0, (int)tpr, 2048, 2048, 2048, st, G);
+    float* y_mine = gather ? y + (size_t)c->rank * tpr * 2048 : y;
+    DT_TRY(launch_gemm(a_op, a->wo, y_mine, 0, (int)tpr, 2048, 2048, 2048, st, G));
+    if (gather && G > 1)
+        DT_TRY(nccl_done(c, n->AllGather(y_mine, y, (size_t)tpr * 2048, ncclFloat32, c->comm, st),
+                         "ncclAllGather(token slices)"));
+    return DT_OK;
+}
+
+int dt_attn_forward_sharded_host(dt_attn* a, const float* x, int B, int T, const int* seq_lens, int gather,
+                                 float* y) {
+    t_last_error.clear();
+    if (!a || !a->shard) return fail(DT_ERR_INVALID_ARGUMENT, "not a sharded handle (dt_attn_create_sharded)");
+    if (B < 0 || T < 0) return fail(DT_ERR_INVALID_ARGUMENT, "negative shape");
+    const long long M = (long long)B * T;
+    const int G = a->shard->comm ? a->shard->comm->world : 1;
+    if (M % G != 0) return fail(DT_ERR_INVALID_ARGUMENT, "B*T = %lld is not divisible by %d ranks", M, G);
+    if (M == 0) return DT_OK;
+    if (!x || !y) return fail(DT_ERR_INVALID_ARGUMENT, "null x/y");
+    DeviceGuard dg;
+    DT_TRY(dg.enter(a->device));
+    if (!a->stream) DT_CUDA(cudaStreamCreateWithFlags(&a->stream, cudaStreamNonBlocking));
+    const long long out_rows = gather ? M : M / G;
+    const size_t xb = align256((size_t)M * 2048 * 4), yb = align256((size_t)out_rows * 2048 * 4);
+    const size_t need = xb + yb + align256((size_t)B * 4);
+    if (a->io_bytes < need) {
+        if (a->io) DT_CUDA(cudaFree(a->io));
+        a->io = nullptr;
+        a->io_bytes = 0;
+        DT_CUDA(cudaMalloc(&a->io, need));
+        a->io_bytes = need;
+    }
+    uint8_t* io = reinterpret_cast<uint8_t*>(a->io);
+    float* dx = reinterpret_cast<float*>(io);
+    float* dy = reinterpret_cast<float*>(io + xb);
+    int* dl = reinterpret_cast<int*>(io + xb + yb);
+    DT_CUDA(cudaMemcpyAsync(dx, x, (size_t)M * 2048 * 4, cudaMemcpyHostToDevice, a->stream));
+    if (seq_lens) DT_CUDA(cudaMemcpyAsync(dl, seq_lens, (size_t)B * 4, cudaMemcpyHostToDevice, a->stream));
+    DT_TRY(dt_attn_forward_sharded(a, dx, B, T, seq_lens ? dl : nullptr, gather, dy, a->stream));
+    DT_CUDA(cudaMemcpyAsync(y, dy, (size_t)out_rows * 2048 * 4, cudaMemcpyDeviceToHost, a->stream));
+    DT_CUDA(cudaStreamSynchronize(a->stream));
+    bool had;
+    return read_device_error(&had);
+}
+
+int dt_attn_create_sharded_from_npy(const char* folder, unsigned index, dt_comm* comm, int exchange, dt_attn** out) {
+    t_last_error.clear();
+    if (!folder || !out) return fail(DT_ERR_INVALID_ARGUMENT, "null argument");
+    std::vector<float> buf[6];
+    DT_TRY(read_attn_npy(folder, index, buf));
+    dt_attn_weights w;
+    w.q_proj = buf[0].data();
+    w.k_proj = buf[1].data();
+    w.v_proj = buf[2].data();
+    w.o_proj = buf[3].data();
+    w.q_norm = buf[4].data();
+    w.k_norm = buf[5].data();
+    w.d_model = 2048;
+    w.n_heads = 16;
+    w.eps = 1e-6f;
+    w.rope_theta = 500000.f;
+    return dt_attn_create_sharded(&w, comm, exchange, out);
 }
 
 int dt_attn_destroy(dt_attn* a) {

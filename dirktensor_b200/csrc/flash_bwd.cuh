@@ -384,19 +384,20 @@ attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_co
             }
             if (!mbar_wait(&sm.dp_full, it & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
-            float dp[2][32];
-            tmem_ld32(tdP + lane_off + hf * 64, dp[0]);
-            tmem_ld32(tdP + lane_off + hf * 64 + 32, dp[1]);
-            tmem_wait_ld();
+            // dP^T one 32-column chunk at a time: with both chunks and P live at
+            // once the math warps ran out of registers and spilled
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
+                float dp[32];
+                tmem_ld32(tdP + lane_off + hf * 64 + ch * 32, dp);
+                tmem_wait_ld();
                 const float* dvec = sm.dvec[s] + (hf * 2 + ch) * 32;
                 uint32_t pd[16], pp[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const float2 d2 = *reinterpret_cast<const float2*>(dvec + 2 * e);
-                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[ch][2 * e] - d2.x) * p.scale,
-                                        pr[ch][2 * e + 1] * (dp[ch][2 * e + 1] - d2.y) * p.scale);
+                    pd[e] = pack_bf16x2(pr[ch][2 * e] * (dp[2 * e] - d2.x) * p.scale,
+                                        pr[ch][2 * e + 1] * (dp[2 * e + 1] - d2.y) * p.scale);
                     pp[e] = pack_bf16x2(pr[ch][2 * e], pr[ch][2 * e + 1]);
                 }
                 // chunk ch of half hf: dS^T into columns [64 hf + 16 ch, +16) and

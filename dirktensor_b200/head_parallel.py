@@ -30,6 +30,9 @@ Two exchange modes:
       step; 2.09 ms for the NCCL path.
   nccl: the flash kernel writes a local [M, Hl*D] buffer and
       torch.distributed.all_to_all_single moves the token slices.
+  allgather: the replicated form -- an all-gather of every rank's per-head
+      outputs ((G-1)/G of the output into every rank), then every rank projects
+      all B*T tokens.  Kept to measure against the token-sliced forms.
 The attention and projection kernels are the CUDA library's.
 """
 from __future__ import annotations
@@ -70,8 +73,8 @@ class HeadParallelAttention:
 
     def __init__(self, wo: torch.Tensor, n_heads: int = 16, head_dim: int = 128,
                  group: Optional[dist.ProcessGroup] = None, exchange: str = "fused"):
-        if exchange not in ("fused", "nccl"):
-            raise ValueError("exchange must be 'fused' or 'nccl'")
+        if exchange not in ("fused", "nccl", "allgather"):
+            raise ValueError("exchange must be 'fused', 'nccl' or 'allgather'")
         self.exchange_mode = exchange
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -131,11 +134,16 @@ class HeadParallelAttention:
 
     # ---- exchange ----------------------------------------------------------
     def exchange(self, o_local: torch.Tensor) -> torch.Tensor:
-        """[M, Hl*D] token-major -> [G, M/G, Hl*D]: plane g = rank g's heads of my tokens."""
+        """[M, Hl*D] token-major -> [G, M/G, Hl*D]: plane g = rank g's heads of my tokens.
+        With exchange 'allgather': -> [G, M, Hl*D], every rank's heads of every token."""
         G = self.world
         M, w = o_local.shape
         if G == 1:
             return o_local
+        if self.exchange_mode == "allgather":
+            full = self._buf("gathered", (G, M, w), o_local.dtype, o_local.device)
+            dist.all_gather_into_tensor(full, o_local, group=self.group)
+            return full
         send = o_local.view(G, M // G, w)
         recv = self._buf("recv", (G, M // G, w), o_local.dtype, o_local.device)
         dist.all_to_all_single(recv, send, group=self.group)
@@ -210,6 +218,9 @@ class HeadParallelAttention:
 
     def forward(self, q, k, v, scale: float, causal: bool = True, events=None,
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """This rank's token slice of y ([B*T/G, d]); with exchange 'allgather'
+        (the replicated form: every rank gathers every head of every token and
+        projects all B*T tokens) the whole y ([B*T, d]) on every rank."""
         B, T, Hl, D = q.shape
         if Hl != self.h1 - self.h0 or D != self.head_dim:
             raise ValueError(f"expected [B, T, {self.h1 - self.h0}, {self.head_dim}] local heads")
@@ -400,18 +411,21 @@ class ShardedOlmoAttention:
         check(lib().dt_attn_create_sharded(ctypes.byref(w), comm.handle, 0 if exchange == "fused" else 1,
                                            ctypes.byref(self._h)))
 
-    def forward(self, x, seq_lens=None, out: Optional[torch.Tensor] = None):
+    def forward(self, x, seq_lens=None, out: Optional[torch.Tensor] = None, gather: bool = False):
+        """gather=False: this rank's token slice [B*T/G, 2048]; gather=True: the
+        whole output [B, T, 2048] on every rank."""
         B, T, d = x.shape
         G = self.comm.world
         if (B * T) % G:
             raise ValueError(f"B*T = {B * T} is not divisible by {G} ranks")
-        y = out if out is not None else torch.empty((B * T // G, d), dtype=torch.float32, device=x.device)
+        shape = (B, T, d) if gather else (B * T // G, d)
+        y = out if out is not None else torch.empty(shape, dtype=torch.float32, device=x.device)
         lens = None
         if seq_lens is not None:
             lens = torch.as_tensor(seq_lens, dtype=torch.int32, device=x.device).contiguous()
         check(lib().dt_attn_forward_sharded(self._h, x.contiguous().data_ptr(), B, T,
-                                            None if lens is None else lens.data_ptr(), y.data_ptr(),
-                                            torch.cuda.current_stream(x.device).cuda_stream))
+                                            None if lens is None else lens.data_ptr(), int(bool(gather)),
+                                            y.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream))
         return y
 
     __call__ = forward

@@ -236,13 +236,25 @@ int dt_comm_destroy(dt_comm* comm);
  * the owners' buffers over NVLink (CUDA IPC; all ranks on one node), 1 = NCCL
  * all-to-all.  Collective: every rank calls it. */
 int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange, dt_attn** out);
-/* Collective forward (every rank, same B, T, seq_lens).  x: [B, T, d_model]
- * fp32 device array (the full input), y: [B*T/G, d_model] fp32 device array
- * (this rank's token slice); B*T must be divisible by G.  seq_lens: device
- * int[B] or NULL (right padding: rows t >= seq_lens[b] of y are zero).
- * Enqueued on `stream`; the NCCL calls use the same stream.  The handle is
- * destroyed with dt_attn_destroy; the communicator outlives it. */
-int dt_attn_forward_sharded(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, float* y, void* stream);
+/* Collective forward (every rank, same B, T, seq_lens, gather).  x:
+ * [B, T, d_model] fp32 device array (the full input).  gather = 0: y is this
+ * rank's token slice [B*T/G, d_model]; gather = 1: y is the whole output
+ * [B, T, d_model] on every rank (the token slices all-gathered in place, what
+ * a caller that adds the residual, as OlmoBlock.cpp:14-16 does, needs).  B*T
+ * must be divisible by G.  seq_lens: device int[B] or NULL (right padding:
+ * rows t >= seq_lens[b] of y are zero).  Enqueued on `stream`; the NCCL calls
+ * use the same stream.  The handle is destroyed with dt_attn_destroy; the
+ * communicator outlives it. */
+int dt_attn_forward_sharded(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, int gather, float* y,
+                            void* stream);
+/* Same with host buffers (x: [B, T, d_model]; y: the slice or, with gather,
+ * the whole output; seq_lens: host int[B] or NULL): copies in, runs the
+ * collective forward on the handle's own stream, copies out, synchronises. */
+int dt_attn_forward_sharded_host(dt_attn* attn, const float* x, int B, int T, const int* seq_lens, int gather,
+                                 float* y);
+/* dt_attn_create_sharded with the weights read from the checkpoint files of
+ * layer `index` in `folder`, as dt_attn_create_from_npy reads them. */
+int dt_attn_create_sharded_from_npy(const char* folder, unsigned index, dt_comm* comm, int exchange, dt_attn** out);
 
 /* ---- full model prefill (configuration 3) -------------------------------
  * Replaces OlmoModel::forward (OlmoModel.cpp:25-48) with OlmoBlock::forward

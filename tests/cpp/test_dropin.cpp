@@ -15,18 +15,26 @@
 //                                     dir/batch.u32, prints "rows cols pad"
 //   test_dropin model <dir> L B T     reads dir/ids.u32 and an L-layer checkpoint from
 //                                     dir, writes dir/logits.f32 (OlmoModel)
+//   test_dropin layer_tp <dir> index B T world rank
+//                                     head-parallel: rank 0 writes the NCCL id to
+//                                     dir/nccl.id, every rank (GPU = rank) makes its
+//                                     communicator, calls set_tensor_parallel, runs the
+//                                     BlockLike forward on dir/x.f32 and writes dir/y<rank>.f32
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
 #include <iostream>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "FlashAttention.h"
 #include "OlmoAttention.h"
 #include "OlmoModel.h"
 #include "Tokens.h"
+#include "dirktensor_b200.h"
 
 template <class X>
 static void read_into(const std::string& path, X& x) {
@@ -96,6 +104,41 @@ int main(int argc, char** argv) {
             block.step(1e-3f);
             write_from(dir + "/y2.f32", block.forward(x));
             block.zero_grad();
+        } else if (mode == "layer_tp" && argc == 8) {
+            const unsigned index = static_cast<unsigned>(std::stoul(argv[3]));
+            const std::size_t B = std::stoul(argv[4]), T = std::stoul(argv[5]);
+            const int world = std::stoi(argv[6]), rank = std::stoi(argv[7]);
+            unsigned char id[128];
+            const std::string idf = dir + "/nccl.id";
+            if (rank == 0) {
+                if (dt_comm_unique_id(id) != DT_OK) throw std::runtime_error(dt_last_error());
+                std::ofstream(idf + ".tmp", std::ios::binary).write(reinterpret_cast<const char*>(id), 128);
+                std::rename((idf + ".tmp").c_str(), idf.c_str());
+            } else {
+                for (int i = 0;; ++i) {  // bounded wait for rank 0's id
+                    std::ifstream f(idf, std::ios::binary);
+                    if (f && f.read(reinterpret_cast<char*>(id), 128)) break;
+                    if (i > 600) throw std::runtime_error("no NCCL id from rank 0");
+                    std::this_thread::sleep_for(std::chrono::milliseconds(100));
+                }
+            }
+            dt_comm* comm = nullptr;
+            if (dt_comm_create(id, world, rank, rank, 60000, &comm) != DT_OK) throw std::runtime_error(dt_last_error());
+            dirktensor_b200::set_tensor_parallel(comm);
+            {
+                xt::xtensor<float, 3> x = xt::empty<float>({B, T, std::size_t(2048)});
+                read_into(dir + "/x.f32", x);
+                BlockLike block(dir, index);
+                const xt::xtensor<float, 3> y = block.forward(x);
+                write_from(dir + "/y" + std::to_string(rank) + ".f32", y);
+                try {  // training stays single-GPU
+                    block.backward(y);
+                    return 4;
+                } catch (const std::runtime_error&) {
+                }
+            }
+            dirktensor_b200::set_tensor_parallel(nullptr);
+            if (dt_comm_destroy(comm) != DT_OK) throw std::runtime_error(dt_last_error());
         } else if (mode == "tokens" && argc >= 5) {
             const uint32_t pad = pad_token_id(argv[3]);
             std::vector<std::string> files(argv + 4, argv + argc);

@@ -23,7 +23,9 @@ def dropin_bin(tmp_path_factory):
     out = str(tmp_path_factory.mktemp("dropin") / "test_dropin")
     subprocess.run(["g++", "-std=c++20", "-O2", "-Wall", "-Wextra", f"-I{CPP}", f"-I{CPP}/compat",
                     f"-I{ROOT}/include", "-o", out, os.path.join(ROOT, "tests", "cpp", "test_dropin.cpp"),
-                    f"-L{CPP}", "-l:libdirktensor_dropin.so", f"-Wl,-rpath,{CPP}"], check=True)
+                    f"-L{CPP}", "-l:libdirktensor_dropin.so", f"-Wl,-rpath,{CPP}",
+                    f"-L{ROOT}/dirktensor_b200", "-l:libdirktensor_b200.so", f"-Wl,-rpath,{ROOT}/dirktensor_b200"],
+                   check=True)
     return out
 
 
@@ -61,6 +63,32 @@ def test_dropin_olmo_attention_block_usage(cuda, dropin_bin, tmp_path):
     # a missing layer surfaces as a C++ exception -> non-zero exit
     r = subprocess.run([dropin_bin, "layer", str(tmp_path), "6", str(B), str(T)], capture_output=True, text=True)
     assert r.returncode == 1 and "cannot open" in r.stderr
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_dropin_olmo_attention_head_parallel(cuda, dropin_bin, tmp_path, world):
+    """dirktensor_b200::set_tensor_parallel(comm): the same OlmoBlock-style owner,
+    unchanged, holds only this rank's heads; every rank's forward returns the
+    whole output.  One process per GPU (rank = GPU), NCCL id through a file."""
+    import torch
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ws = layer_weights(34)
+    for n, w in zip(["q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"], ws):
+        np.save(tmp_path / f"model.layers.3.self_attn.{n}.weight.npy", w)
+    B, T = 2, 320
+    x = randn(35, (B, T, 2048))
+    x.tofile(tmp_path / "x.f32")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([dropin_bin, "layer_tp", str(tmp_path), "3", str(B), str(T), str(world), str(r)],
+                              env=env) for r in range(world)]
+    for p in procs:
+        assert p.wait(timeout=300) == 0
+    ref = oracle.attention_layer(x, *ws)
+    for r in range(world):
+        y = np.fromfile(tmp_path / f"y{r}.f32", np.float32).reshape(B, T, 2048)
+        assert rel_l2(y, ref) < TOL_LAYER_REL_L2, r
 
 
 def test_dropin_olmo_attention_training_calls(cuda, dropin_bin, tmp_path):

@@ -45,7 +45,7 @@ def _check(case, y_full):
         assert not np.any(y_full[b, n:])
 
 
-def _sharded(rank, world, dev, case, exchange, comm):
+def _sharded(rank, world, dev, case, exchange, comm, gather=False):
     import torch
 
     from dirktensor_b200.head_parallel import ShardedOlmoAttention
@@ -53,7 +53,7 @@ def _sharded(rank, world, dev, case, exchange, comm):
     x, w, lens = _inputs(case)
     layer = ShardedOlmoAttention(*w, comm=comm, exchange=exchange)
     xd = torch.from_numpy(x).to(dev)
-    ys = [layer.forward(xd, seq_lens=lens).cpu().numpy() for _ in range(3)]  # both receive buffers
+    ys = [layer.forward(xd, seq_lens=lens, gather=gather).cpu().numpy() for _ in range(3)]  # both receive buffers
     torch.cuda.synchronize(dev)
     layer.close()
     for y in ys[1:]:
@@ -68,7 +68,7 @@ def test_sharded_layer_world1_vs_oracle(cuda, case):
 
     comm = Communicator(1, 0, Communicator.unique_id(), 0, timeout_ms=60000)
     try:
-        y = _sharded(0, 1, cuda, case, "fused", comm)
+        y = _sharded(0, 1, cuda, case, "fused", comm, gather=(case == "varlen"))
     finally:
         comm.close()
     dt.check_device_error()
@@ -93,7 +93,7 @@ def test_sharded_layer_rejected_by_single_gpu_calls(cuda):
     dt.check_device_error()
 
 
-def _worker(rank, world, port, out_dir, impl, case, exchange):
+def _worker(rank, world, port, out_dir, impl, case, exchange, gather=False):
     import torch
     import torch.distributed as dist
 
@@ -106,7 +106,7 @@ def _worker(rank, world, port, out_dir, impl, case, exchange):
         from dirktensor_b200.head_parallel import Communicator
 
         comm = Communicator.from_process_group(timeout_ms=60000)
-        y = _sharded(rank, world, dev, case, exchange, comm)
+        y = _sharded(rank, world, dev, case, exchange, comm, gather)
         comm.close()
     else:
         from dirktensor_b200.head_parallel import HeadParallelAttentionLayer
@@ -124,10 +124,12 @@ def _worker(rank, world, port, out_dir, impl, case, exchange):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("impl,case,exchange", [("capi", "config0", "fused"), ("capi", "varlen", "fused"),
-                                                ("capi", "varlen", "nccl"), ("torch", "config0", "fused"),
-                                                ("torch", "varlen", "nccl")])
-def test_sharded_layer_world2(cuda, tmp_path, impl, case, exchange):
+@pytest.mark.parametrize("impl,case,exchange,gather", [("capi", "config0", "fused", False),
+                                                       ("capi", "varlen", "fused", True),
+                                                       ("capi", "varlen", "nccl", False),
+                                                       ("torch", "config0", "fused", False),
+                                                       ("torch", "varlen", "nccl", False)])
+def test_sharded_layer_world2(cuda, tmp_path, impl, case, exchange, gather):
     import torch
     import torch.multiprocessing as mp
 
@@ -138,11 +140,15 @@ def test_sharded_layer_world2(cuda, tmp_path, impl, case, exchange):
     port = s.getsockname()[1]
     s.close()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), impl, case, exchange)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), impl, case, exchange, gather))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    y = np.concatenate([np.load(tmp_path / f"y{r}.npy") for r in range(2)])
-    _check(case, y)
+    if gather:  # every rank holds the whole output
+        for r in range(2):
+            _check(case, np.load(tmp_path / f"y{r}.npy"))
+    else:
+        _check(case, np.concatenate([np.load(tmp_path / f"y{r}.npy") for r in range(2)]))
