@@ -17,7 +17,8 @@ def driver(tmp_path_factory):
     out = str(tmp_path_factory.mktemp("tok") / "test_dropin")
     subprocess.run(["g++", "-std=c++20", "-O2", f"-I{CPP}", f"-I{CPP}/compat", f"-I{ROOT}/include", "-o", out,
                     os.path.join(ROOT, "tests", "cpp", "test_dropin.cpp"), f"-L{CPP}", "-l:libdirktensor_dropin.so",
-                    f"-Wl,-rpath,{CPP}"], check=True)
+                    f"-Wl,-rpath,{CPP}", f"-L{ROOT}/dirktensor_b200", "-l:libdirktensor_b200.so",
+                    f"-Wl,-rpath,{ROOT}/dirktensor_b200"], check=True)
     return out
 
 
