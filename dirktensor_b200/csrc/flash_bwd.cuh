@@ -384,13 +384,18 @@ attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_co
             }
             if (!mbar_wait(&sm.dp_full, it & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
-            // dP^T one 32-column chunk at a time: with both chunks and P live at
-            // once the math warps ran out of registers and spilled
+            // dP^T one 32-column chunk at a time (with both chunks and P live at
+            // once the math warps ran out of registers and spilled).  Chunk ch of
+            // half hf: dS^T goes to columns [64 hf + 16 ch, +16) and P^T to
+            // [64 hf + 32 + 16 ch, +16) of dP^T.  P^T of chunk 0 lands in chunk 1's
+            // columns, so it is stored only after chunk 1 has been loaded.
+            uint32_t pp0[16];
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
                 float dp[32];
                 tmem_ld32(tdP + lane_off + hf * 64 + ch * 32, dp);
                 tmem_wait_ld();
+                if (ch == 1) tmem_st16(tdP + lane_off + hf * 64 + 32, pp0);
                 const float* dvec = sm.dvec[s] + (hf * 2 + ch) * 32;
                 uint32_t pd[16], pp[16];
 #pragma unroll
@@ -400,10 +405,13 @@ attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_co
                                         pr[ch][2 * e + 1] * (dp[2 * e + 1] - d2.y) * p.scale);
                     pp[e] = pack_bf16x2(pr[ch][2 * e], pr[ch][2 * e + 1]);
                 }
-                // chunk ch of half hf: dS^T into columns [64 hf + 16 ch, +16) and
-                // P^T into [64 hf + 32 + 16 ch, +16) of dP^T, all read above
                 tmem_st16(tdP + lane_off + hf * 64 + ch * 16, pd);
-                tmem_st16(tdP + lane_off + hf * 64 + 32 + ch * 16, pp);
+                if (ch == 0) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) pp0[e] = pp[e];
+                } else {
+                    tmem_st16(tdP + lane_off + hf * 64 + 48, pp);
+                }
             }
             tmem_wait_st();
             tc_fence_before();
