@@ -1686,7 +1686,7 @@ int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int*
         DT_CUDA(cudaMalloc(&a->ws, need));
         a->ws_bytes = need;
     }
-    if (sh->exchange == 0) DT_TRY(shard_setup_exchange(a, M, st));
+    if (sh->exchange == 0 && G > 1) DT_TRY(shard_setup_exchange(a, M, st));
     uint8_t* p = reinterpret_cast<uint8_t*>(a->ws);
     void* xb = p;
     p += align256(M * 2048 * 2);
