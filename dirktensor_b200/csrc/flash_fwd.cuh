@@ -42,7 +42,6 @@ constexpr int kStages = 4;
 constexpr int kTileBytes = kBM * kD * 2;   // 32 KB
 constexpr int kHalfBytes = kTileBytes / 2; // 128 rows x 128 B (one swizzle span of 64 bf16)
 constexpr int kThreads = 384;  // 3 warpgroups: registers are granted per warpgroup
-constexpr int kSub = 64;       // keys per softmax sub-step (half a K/V tile)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Of every 16 column pairs of an unmasked S tile, this many compute 2^x on the
 // FMA pipe (exp2_poly_pair) instead of the MUFU.  Measured on B200 with 0, 2, 4
@@ -90,19 +89,15 @@ struct __align__(1024) Smem {
     uint64_t q_full;
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
-    uint64_t s_full[kQTiles][2];   // S buffer (tile, j % 2) holds S_i(j)
-    uint64_t p_full[kQTiles][2];   // P_i(j) stored in S buffer (tile, j % 2)
-    uint64_t pv_done[kQTiles][2];  // PV_i(j) complete (j % 2)
+    uint64_t s_full[kQTiles];
+    uint64_t p_full[kQTiles];
     uint64_t o_full[kQTiles];
     uint64_t mma_done;
     uint32_t tmem_base;
 };
 
 // Wait-site ids reported with a timeout.
-enum : unsigned { kSiteQ = 1, kSiteKvEmpty, kSiteKvFull, kSiteS, kSiteP, kSiteO, kSiteDone, kSitePv };
-
-// TMEM column of S buffer b (0, 1) of Q tile i: 64 fp32 columns each.
-__device__ __forceinline__ constexpr uint32_t s_col(int i, int b) { return (uint32_t)(2 * i + b) * kSub; }
+enum : unsigned { kSiteQ = 1, kSiteKvEmpty, kSiteKvFull, kSiteS, kSiteP, kSiteO, kSiteDone };
 
 // Writes 32 consecutive output columns [col0, col0+32) of row (b, t, h), each multiplied by `mul`.
 __device__ __forceinline__ void store_chunk(const Params& p, int b, int t, int h, int col0, const float* v, float mul) {
@@ -176,11 +171,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
             mbar_init(&sm.kv_empty[s], 1);
         }
         for (int i = 0; i < kQTiles; ++i) {
-            for (int b = 0; b < 2; ++b) {
-                mbar_init(&sm.s_full[i][b], 1);
-                mbar_init(&sm.p_full[i][b], 4);
-                mbar_init(&sm.pv_done[i][b], 1);
-            }
+            mbar_init(&sm.s_full[i], 1);
+            mbar_init(&sm.p_full[i], 4);
             mbar_init(&sm.o_full[i], 1);
         }
         mbar_init(&sm.mma_done, 1);
@@ -231,80 +223,60 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         }
     } else if (warp == 9) {
         // ------------------------------ MMA issuer --------------------------
-        // Sub-step j of Q tile i covers keys [64j, 64j+64): K/V tile j/2, half j%2.
-        // Issue order per sub-step j, for i = 0, 1:  [P_i(j) ready] PV_i(j), S_i(j+2).
-        // S_i(j+1) was issued one sub-step earlier, so it is (or soon will be)
-        // in TMEM when softmax i finishes sub-step j: the softmax never waits
-        // for the PV/S products of its own last hand-off.  S_i(j+2) reuses the
-        // buffer that held P_i(j); tcgen05 ops of this thread execute in issue
-        // order, so it cannot overwrite P_i(j) before PV_i(j) has read it.
         if (lane == 0 && nkv > 0) {
-            constexpr uint32_t idesc_qk = umma_idesc_bf16(kBM, kSub, 0, 0);
+            constexpr uint32_t idesc_qk = umma_idesc_bf16(kBM, kBN, 0, 0);
             constexpr uint32_t idesc_pv = umma_idesc_bf16(kBM, kD, 0, 1);
-            const int nsub_t[kQTiles] = {2 * n_t0, 2 * n_t1};
-            const int nsub = 2 * nkv;
             bool ok = mbar_wait_sleep(&sm.q_full, 0, kSiteQ);
-            auto k_stage = [](int t) { return (2 * t) % kStages; };
-            auto v_stage = [](int t) { return (2 * t + 1) % kStages; };
-            auto k_phase = [](int t) { return (uint32_t)(((2 * t) / kStages) & 1); };
-            auto v_phase = [](int t) { return (uint32_t)(((2 * t + 1) / kStages) & 1); };
-            auto issue_s = [&](int i, int j) {
-                // S_i(j) = Q_i K[64j .. 64j+64)^T into S buffer (i, j%2): 8 products of K=16
-                const uint32_t kaddr = smem_u32(sm.kv[k_stage(j >> 1)]) + (uint32_t)(j & 1) * (kSub * 128);
+            auto stage_of = [](int L) { return L % kStages; };
+            auto phase_of = [](int L) { return (uint32_t)((L / kStages) & 1); };
+            auto issue_s = [&](int i, int L) {
+                const uint32_t kaddr = smem_u32(sm.kv[stage_of(L)]);
                 const uint32_t qaddr = smem_u32(sm.q[0]) + (uint32_t)i * kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-                    umma_ss(tmem + s_col(i, j & 1), umma_desc_sw128(qaddr + off, 16, 1024),
+                    umma_ss(tmem + i * 128, umma_desc_sw128(qaddr + off, 16, 1024),
                             umma_desc_sw128(kaddr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
                 }
-                umma_commit(&sm.s_full[i][j & 1]);
+                umma_commit(&sm.s_full[i]);
             };
-            auto issue_pv = [&](int i, int j) {
-                // O_i += P_i(j) V[64j .. 64j+64): P from TMEM (bf16 pairs, 32 columns),
-                // V MN-major: 64-dim halves kHalfBytes apart (LBO), 8-key groups 1024 B
-                // apart (SBO); 16 keys (2048 B) per product
-                const uint32_t vaddr = smem_u32(sm.kv[v_stage(j >> 1)]) + (uint32_t)(j & 1) * (kSub * 128);
+            auto issue_pv = [&](int i, int L, bool acc) {
+                const uint32_t vaddr = smem_u32(sm.kv[stage_of(L)]);
 #pragma unroll
-                for (int kk = 0; kk < kSub / 16; ++kk)
-                    umma_ts(tmem + 256 + i * 128, tmem + s_col(i, j & 1) + kk * 8,
+                for (int kk = 0; kk < kBN / 16; ++kk) {
+                    // V is MN-major for this product: 64-dim halves kHalfBytes apart (LBO),
+                    // 8-key groups 1024 B apart (SBO); 16 keys per instruction.
+                    umma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8,
                             umma_desc_sw128(vaddr + kk * 2048, kHalfBytes, 1024), idesc_pv,
-                            (j > 0 || kk > 0) ? 1u : 0u);
+                            (acc || kk > 0) ? 1u : 0u);
+                }
             };
-            if (ok) ok = mbar_wait_sleep(&sm.kv_full[k_stage(0)], k_phase(0), kSiteKvFull);
+            if (ok) ok = mbar_wait_sleep(&sm.kv_full[stage_of(0)], phase_of(0), kSiteKvFull);
             if (ok) {
                 tc_fence_after();
-                for (int i = 0; i < kQTiles; ++i)
-                    for (int j = 0; j < 2 && j < nsub_t[i]; ++j) issue_s(i, j);
-                umma_commit(&sm.kv_empty[k_stage(0)]);  // K tile 0 is read by S_i(0), S_i(1) only
+                if (n_t0 > 0) issue_s(0, 0);
+                if (n_t1 > 0) issue_s(1, 0);
+                umma_commit(&sm.kv_empty[stage_of(0)]);
             }
-            for (int j = 0; ok && j < nsub; ++j) {
-                const int t = j >> 1;
-                if ((j & 1) == 0) {
-                    // V tile t for PV(j), PV(j+1); K tile t+1 for S(j+2), S(j+3)
-                    ok = mbar_wait_sleep(&sm.kv_full[v_stage(t)], v_phase(t), kSiteKvFull);
-                    if (ok && j + 2 < nsub)
-                        ok = mbar_wait_sleep(&sm.kv_full[k_stage(t + 1)], k_phase(t + 1), kSiteKvFull);
-                    if (!ok) break;
-                }
+            for (int j = 0; ok && j < nkv; ++j) {
+                const int LV = 2 * j + 1, LK = 2 * j + 2;
+                const bool next_k = (j + 1) < nkv;
+                ok = mbar_wait_sleep(&sm.kv_full[stage_of(LV)], phase_of(LV), kSiteKvFull);
+                if (ok && next_k) ok = mbar_wait_sleep(&sm.kv_full[stage_of(LK)], phase_of(LK), kSiteKvFull);
+                if (!ok) break;
                 tc_fence_after();
                 for (int i = 0; i < kQTiles; ++i) {
-                    if (j >= nsub_t[i]) continue;
-                    if (!mbar_wait_sleep(&sm.p_full[i][j & 1], (uint32_t)((j >> 1) & 1), kSiteP)) {
-                        ok = false;
-                        break;
-                    }
+                    const int ni = (i == 0) ? n_t0 : n_t1;
+                    if (j >= ni) continue;
+                    if (!mbar_wait_sleep(&sm.p_full[i], j & 1, kSiteP)) { ok = false; break; }
                     tc_fence_after();
-                    issue_pv(i, j);
-                    umma_commit(&sm.pv_done[i][j & 1]);
-                    if (j + 2 < nsub_t[i]) issue_s(i, j + 2);
-                    else if (j + 1 == nsub_t[i]) umma_commit(&sm.o_full[i]);
+                    issue_pv(i, LV, j > 0);
+                    if (j + 1 < ni) issue_s(i, LK);
+                    else umma_commit(&sm.o_full[i]);
                 }
                 if (!ok) break;
-                if (j & 1) {
-                    umma_commit(&sm.kv_empty[v_stage(t)]);                      // both halves of V tile t
-                    if (j + 1 < nsub) umma_commit(&sm.kv_empty[k_stage(t + 1)]);  // both halves of K tile t+1
-                }
+                umma_commit(&sm.kv_empty[stage_of(LV)]);
+                if (next_k) umma_commit(&sm.kv_empty[stage_of(LK)]);
             }
             // All issued tcgen05 work must be complete before TMEM is released.
             umma_commit(&sm.mma_done);
@@ -347,40 +319,40 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         const int qt = q0 + i * kBM;
         const int q_pos = qt + r;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + lane_off + i * 128;
         const uint32_t tO = tmem + lane_off + 256 + i * 128;
-        const int n = (i == 0) ? n_t0 : n_t1;  // K/V tiles of this Q tile
-        const int nsub = 2 * n;
+        const int n = (i == 0) ? n_t0 : n_t1;
         float m_run = -INFINITY, l_run = 0.f, mx = -INFINITY;
         bool ok = true;
-        for (int j = 0; j < nsub; ++j) {
-            const int bsel = j & 1;
-            const uint32_t tS = tmem + lane_off + s_col(i, bsel);
-            if (!mbar_wait_sleep(&sm.s_full[i][bsel], (uint32_t)((j >> 1) & 1), kSiteS)) { ok = false; break; }
+        for (int j = 0; j < n; ++j) {
+            if (!mbar_wait_sleep(&sm.s_full[i], j & 1, kSiteS)) { ok = false; break; }
             tc_fence_after();
-            float s[kSub];
+            float s[128];
             tmem_ld32(tS + 0, *reinterpret_cast<float(*)[32]>(s + 0));
             tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+            tmem_ld32(tS + 64, *reinterpret_cast<float(*)[32]>(s + 64));
+            tmem_ld32(tS + 96, *reinterpret_cast<float(*)[32]>(s + 96));
             tmem_wait_ld();
-            const int k0 = j * kSub;
-            const bool diag = p.causal && (k0 + kSub - 1 > qt);
-            const bool tail = (k0 + kSub > Tb);
+            const int k0 = j * kBN;
+            const bool diag = p.causal && (k0 + kBN - 1 > qt);
+            const bool tail = (k0 + kBN > Tb);
             if (diag || tail) {
                 const int lim = p.causal ? min(q_pos, Tb - 1) : (Tb - 1);
 #pragma unroll
-                for (int e = 0; e < kSub; ++e)
+                for (int e = 0; e < 128; ++e)
                     if (k0 + e > lim) s[e] = -INFINITY;
             }
-            // Row max as 4 independent chains over 16-column slices, then a short
-            // combine: one 32-deep chain of dependent max ops is latency-bound.
-            float pm[4];
+            // Row max as 8 independent chains over 16-column slices, then a short
+            // combine: a single 64-deep chain of dependent max ops is latency-bound.
+            float pm[8];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
+            for (int g = 0; g < 8; ++g) {
                 float a = fmax3(s[16 * g], s[16 * g + 1], s[16 * g + 2]);
 #pragma unroll
                 for (int e = 3; e < 15; e += 2) a = fmax3(a, s[16 * g + e], s[16 * g + e + 1]);
                 pm[g] = fmaxf(a, s[16 * g + 15]);
             }
-            const float rmax = fmaxf(fmax3(pm[0], pm[1], pm[2]), pm[3]);
+            const float rmax = fmaxf(fmax3(pm[0], pm[1], pm[2]), fmax3(fmax3(pm[3], pm[4], pm[5]), pm[6], pm[7]));
             mx = fmaxf(mx, rmax);
             const float m_cand = rmax * p.scale_log2;
             float alpha = 1.f;
@@ -393,13 +365,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
                         alpha = ex2_approx(m_run - m_cand);
                         m_run = m_cand;
                     }
-                    // O_i must hold every earlier product before it is rescaled:
-                    // PV_i(j-1) is the last one issued (tcgen05 ops complete in order).
-                    if (!mbar_wait_sleep(&sm.pv_done[i][(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), kSitePv)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
 #pragma unroll 1
                     for (int cc = 0; cc < 8; ++cc) {
                         float o[16];
@@ -415,10 +380,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
             // packed f32x2 pairs; ex2 stays per element (MUFU).
             const uint64_t c2 = f2_pack(p.scale_log2, p.scale_log2);
             const uint64_t nm2 = f2_pack(-m_run, -m_run);
-            uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+            // one packed partial sum per 32-column chunk: four independent chains
+            uint64_t sum2[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
             const bool masked = diag || tail;
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
+            for (int cc = 0; cc < 4; ++cc) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
@@ -436,12 +402,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
                 tmem_st16(tS + cc * 16, pk);
             }
             float sum_lo, sum_hi;
-            f2_unpack(f2_add(sum2[0], sum2[1]), sum_lo, sum_hi);
+            f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])), sum_lo, sum_hi);
             const float sum = sum_lo + sum_hi;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.p_full[i][bsel]);
+            if (lane == 0) mbar_arrive(&sm.p_full[i]);
             l_run = l_run * alpha + sum;
         }
         // ---- epilogue: O / l and the statistics -------------------------
