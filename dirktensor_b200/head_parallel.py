@@ -141,9 +141,9 @@ class HeadParallelAttention:
         if G == 1:
             return o_local
         if self.exchange_mode == "allgather":
-            full = self._buf("gathered", (G, M, w), o_local.dtype, o_local.device)
-            dist.all_gather_into_tensor(full, o_local, group=self.group)
-            return full
+            full = self._buf("gathered", (G * M, w), o_local.dtype, o_local.device)
+            dist.all_gather_into_tensor(full, o_local.contiguous(), group=self.group)
+            return full.view(G, M, w)
         send = o_local.view(G, M // G, w)
         recv = self._buf("recv", (G, M // G, w), o_local.dtype, o_local.device)
         dist.all_to_all_single(recv, send, group=self.group)

@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, B, T, H, out_dir):
+def _worker(rank, world, port, B, T, H, out_dir, exchange="nccl"):
     import torch.distributed as dist
 
     import oracle
@@ -51,23 +51,26 @@ def _worker(rank, world, port, B, T, H, out_dir):
     q, k, v = qkv(5, B, T, H)
     wo = randn(6, (2048 // 16 * H, 2048 // 16 * H), 0.02)
     h0, h1 = head_range(rank, world, H)
-    hp = CpuHeadParallel(torch.from_numpy(wo), n_heads=H, head_dim=128)
+    hp = CpuHeadParallel(torch.from_numpy(wo), n_heads=H, head_dim=128, exchange=exchange)
     y = hp.forward(*(torch.from_numpy(np.ascontiguousarray(a[:, :, h0:h1])) for a in (q, k, v)), SCALE, True)
-    t0, t1 = token_range(rank, world, B * T)
+    t0, t1 = token_range(rank, world, B * T) if exchange != "allgather" else (0, B * T)
     np.save(os.path.join(out_dir, f"y{rank}.npy"), y.numpy())
     np.save(os.path.join(out_dir, f"range{rank}.npy"), np.array([t0, t1]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_head_parallel_exchange_matches_unsharded(tmp_path, world):
+@pytest.mark.parametrize("world,exchange", [(2, "nccl"), (4, "nccl"), (2, "allgather"), (4, "allgather")])
+def test_head_parallel_exchange_matches_unsharded(tmp_path, world, exchange):
+    """Token-sliced all-to-all: each rank gets its token slice; replicated
+    all-gather: every rank gets the whole output."""
     import oracle
 
     B, T, H = 2, 96, 8
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, B, T, H, str(tmp_path))) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, T, H, str(tmp_path), exchange))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
