@@ -351,7 +351,7 @@ def main():
     f_flash_rank = F_ATTN / world
     achieved = f_flash_rank / (ms_flash * 1e-3) / 1e12
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "flash_fwd_traffic.json")
+    tpath = os.path.join(ROOT, "profiles", "attn_fwd_traffic.json")
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:

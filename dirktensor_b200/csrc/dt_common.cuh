@@ -351,14 +351,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// Packs (lo, hi) into one 32-bit word of two bf16 by truncation (the upper
-// halves of the two fp32 words, one byte permute); `lo` lands in bits [0,16).
-__device__ __forceinline__ uint32_t bf16x2_trunc(float lo, float hi) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(__float_as_uint(lo)), "r"(__float_as_uint(hi)));
-    return r;
-}
-
 // Packs (lo, hi) into one 32-bit word of two bf16 (round to nearest even);
 // `lo` lands in bits [0,16).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -52,9 +52,6 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #define DT_FLASH_EMU_PAIRS 0
 #endif
 constexpr int kEmuPairs = DT_FLASH_EMU_PAIRS;
-#ifndef DT_FLASH_P_TRUNC
-#define DT_FLASH_P_TRUNC 0
-#endif
 
 struct Params {
     int B, T, H;
@@ -399,16 +396,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
                         p0 = ex2_approx(x0);
                         p1 = ex2_approx(x1);
                     }
-#if DT_FLASH_P_TRUNC
-                    // bf16 pair by one byte permute (truncation); the row sum adds the same
-                    // truncated values, so O / l weighs V with exactly the P it multiplied
-                    pk[e] = bf16x2_trunc(p0, p1);
-                    sum2[cc] = f2_add(sum2[cc], f2_pack(__uint_as_float(pk[e] << 16),
-                                                        __uint_as_float(pk[e] & 0xffff0000u)));
-#else
                     sum2[cc] = f2_add(sum2[cc], f2_pack(p0, p1));
                     pk[e] = pack_bf16x2(p0, p1);
-#endif
                 }
                 tmem_st16(tS + cc * 16, pk);
             }
