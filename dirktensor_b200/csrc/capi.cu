@@ -166,6 +166,14 @@ constexpr size_t kGemm2Smem = sizeof(dt::gemm2::Smem) + 1024;
 // GEMMs with at least this many rows run on SM pairs (gemm2sm.cuh); measured on
 // B200 at the model's shapes the pair kernel is 18-57 % faster than the one-SM
 // kernel, which remains for row counts below one pair tile's half.
+// Attention on grids of fewer 256-row blocks than SMs runs one 128-row Q tile per CTA.
+#ifndef DT_FLASH_SMALL_GRID_ONE_TILE
+#define DT_FLASH_SMALL_GRID_ONE_TILE 1
+#endif
+// Pair tiles must give at least this many tiles per 100 SM pairs for the pair kernel.
+#ifndef DT_GEMM_PAIR_MIN_FILL
+#define DT_GEMM_PAIR_MIN_FILL 100
+#endif
 #ifndef DT_GEMM_2SM_MIN_M
 #define DT_GEMM_2SM_MIN_M 256
 #endif
@@ -343,17 +351,21 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     p.B = B;
     p.T = T;
     p.H = H;
-    p.nblk = (T + 255) / 256;
     {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
+        const int BH = B * H;
+        // One Q tile per CTA (128-row work items) when 256-row blocks would not
+        // give every SM a CTA (short sequences, few heads): twice the CTAs, each
+        // half as long.
+        p.qtiles = (DT_FLASH_SMALL_GRID_ONE_TILE && (long long)BH * ((T + 255) / 256) < sms) ? 1 : 2;
+        p.nblk = (T + 128 * p.qtiles - 1) / (128 * p.qtiles);
         // Scheduling groups of (b, h) pairs.  When the K/V of all heads fit in L2
         // (<= 64 MB of bf16) one group keeps a global heaviest-first order.
         // Otherwise each group holds about two waves of blocks -- enough to fill
         // the GPU, few enough heads that their K/V stay in L2 -- and the groups
         // are sized evenly so the last one is not a short tail.
-        int dev = 0;
-        cudaGetDevice(&dev);
-        const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
-        const int BH = B * H;
         const double kv_bytes = (double)BH * T * 128 * 2 * 2;
         if (kv_bytes <= 64.0 * 1024 * 1024) {
             p.group = BH;
@@ -463,7 +475,8 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
     const long long wide_tiles = (long long)((M + 127) / 128) * ((N + 255) / 256);
     // (MN-major operands run on the one-SM kernel)
-    const bool pair = M >= DT_GEMM_2SM_MIN_M && pair_tiles >= nsm / 2 && !a_mn && !b_mn;
+    const bool pair = M >= DT_GEMM_2SM_MIN_M && N >= 256 && pair_tiles * 100 >= (long long)(nsm / 2) * DT_GEMM_PAIR_MIN_FILL &&
+                      !a_mn && !b_mn;
     const bool narrow = !pair && epilogue != dt::gemm::kSwiGLU && wide_tiles < nsm;
     const int bn = narrow ? dt::gemm::kNarrowBN : dt::gemm::kBN;
     // boxes: 128 rows of A and bn rows of B per CTA, or 128 and 128 on SM pairs

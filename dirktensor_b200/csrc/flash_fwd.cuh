@@ -55,7 +55,9 @@ constexpr int kEmuPairs = DT_FLASH_EMU_PAIRS;
 
 struct Params {
     int B, T, H;
-    int nblk;               // 256-row blocks per (b, h)
+    int nblk;               // work items per (b, h): blocks of qtiles * 128 rows
+    int qtiles;             // Q tiles per CTA: 2 (256-row blocks), or 1 when 256-row
+                            // blocks would leave SMs idle (short sequences)
     int group;              // (b, h) pairs per scheduling group (L2-resident K/V working set)
     int causal;
     float scale;            // the caller's scale (reference: 1/sqrt(head_dim))
@@ -157,11 +159,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
     const int b = bh / p.H;
     const int h = bh % p.H;
     const int Tb = p.seq_lens ? min(max(p.seq_lens[b], 0), p.T) : p.T;
-    const int q0 = c * (kQTiles * kBM);
+    const int q0 = c * (p.qtiles * kBM);
     const int nkv_all = (Tb + kBN - 1) / kBN;
     // KV tiles visited by Q tile 0 and Q tile 1 (0 when the tile starts past the sequence)
-    const int n_t0 = (q0 < Tb) ? (p.causal ? min(2 * c + 1, nkv_all) : nkv_all) : 0;
-    const int n_t1 = (q0 + kBM < Tb) ? (p.causal ? min(2 * c + 2, nkv_all) : nkv_all) : 0;
+    const int n_t0 = (q0 < Tb) ? (p.causal ? min(p.qtiles * c + 1, nkv_all) : nkv_all) : 0;
+    const int n_t1 = (p.qtiles > 1 && q0 + kBM < Tb) ? (p.causal ? min(2 * c + 2, nkv_all) : nkv_all) : 0;
     const int nkv = max(n_t0, n_t1);
 
     if (threadIdx.x == 0) {
@@ -196,8 +198,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         // ------------------------------ TMA producer ------------------------
         if (lane == 0 && nkv > 0) {
             if (!p.q_f32) {
-                mbar_arrive_expect_tx(&sm.q_full, kQTiles * kTileBytes);
-                for (int i = 0; i < kQTiles; ++i)
+                mbar_arrive_expect_tx(&sm.q_full, p.qtiles * kTileBytes);
+                for (int i = 0; i < p.qtiles; ++i)
                     for (int hf = 0; hf < 2; ++hf)
                         tma_load_4d(sm.q[i] + hf * kHalfBytes, &tmap_q, &sm.q_full, hf * 64, h, q0 + i * kBM, b);
             }
@@ -296,8 +298,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
             const uint32_t qs = smem_u32(sm.q[warp >> 2]);
             const int chunk = lane >> 1;  // 16-byte chunk (8 dims) of this lane's 4 dims
             const uint32_t col = (uint32_t)(chunk >> 3) * kHalfBytes + (uint32_t)(lane & 1) * 8;
+            // (a disabled second tile loads nothing)
 #pragma unroll 32
-            for (int rr = 0; rr < 32; ++rr) {
+            for (int rr = 0; rr < 32 && (warp >> 2) < p.qtiles; ++rr) {
                 const int row = (warp & 3) * 32 + rr;
                 const int t = q0 + (warp >> 2) * kBM + row;
                 float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -411,8 +414,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
             l_run = l_run * alpha + sum;
         }
         // ---- epilogue: O / l and the statistics -------------------------
-        // Rows past the sequence length (varlen padding) are written as zeros.
-        const bool row_in = q_pos < p.T;
+        // Rows past the sequence length (varlen padding) are written as zeros; a
+        // disabled second tile (qtiles == 1) owns no rows.
+        const bool row_in = i < p.qtiles && q_pos < p.T;
         const bool row_valid = q_pos < Tb;
         bool have_o = false;
         if (n > 0 && ok) have_o = mbar_wait_sleep(&sm.o_full[i], 0, kSiteO);
