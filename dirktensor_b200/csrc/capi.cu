@@ -708,15 +708,19 @@ int nccl_done(dt_comm* c, ncclResult_t r, const char* what) {
                 r = st;
                 break;
             }
-            const auto ms =
-                std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
-            if (ms > c->timeout_ms) {
+            const auto us =
+                std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+            if (us > 1000LL * c->timeout_ms) {
                 n.CommAbort(c->comm);
                 c->comm = nullptr;
                 return fail(DT_ERR_TIMEOUT, "%s did not complete within %d ms; the communicator was aborted", what,
                             c->timeout_ms);
             }
-            std::this_thread::sleep_for(std::chrono::microseconds(100));
+            // An enqueue finishes within microseconds: spin first (the GPU may be
+            // idle until the next launch is queued), sleep only for long waits
+            // (communicator set-up).
+            if (us < 2000) std::this_thread::yield();
+            else std::this_thread::sleep_for(std::chrono::microseconds(100));
         }
     }
     if (r != ncclSuccess) return fail(DT_ERR_NCCL, "%s: %s", what, n.GetErrorString(r));
