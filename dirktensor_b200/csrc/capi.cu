@@ -166,6 +166,10 @@ constexpr size_t kGemm2Smem = sizeof(dt::gemm2::Smem) + 1024;
 // GEMMs with at least this many rows run on SM pairs (gemm2sm.cuh); measured on
 // B200 at the model's shapes the pair kernel is 18-57 % faster than the one-SM
 // kernel, which remains for row counts below one pair tile's half.
+// QK-norm/RoPE prologue: 0 = one CTA per token; n > 0 = a persistent grid of n CTAs per SM.
+#ifndef DT_PROLOGUE_PERSISTENT
+#define DT_PROLOGUE_PERSISTENT 0
+#endif
 // Attention on grids of fewer 256-row blocks than SMs runs one 128-row Q tile per CTA.
 #ifndef DT_FLASH_SMALL_GRID_ONE_TILE
 #define DT_FLASH_SMALL_GRID_ONE_TILE 1
@@ -555,7 +559,17 @@ int launch_prologue(const float* q, const float* k, const float* v, long long ld
     p.T = T;
     p.eps = eps;
     if (M > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "too many rows");
+#if DT_PROLOGUE_PERSISTENT
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
+        const long long grid = std::min<long long>(M, (long long)sms * DT_PROLOGUE_PERSISTENT);
+        dt::elem::qk_norm_rope_loop_kernel<<<(unsigned)grid, dt::elem::kPrologueThreads, 0, st>>>(p, M);
+    }
+#else
     dt::elem::qk_norm_rope_kernel<<<(unsigned)M, dt::elem::kPrologueThreads, 0, st>>>(p);
+#endif
     DT_CUDA(cudaGetLastError());
     return DT_OK;
 }

@@ -153,6 +153,95 @@ qk_norm_rope_kernel(const PrologueParams p) {
     *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) = vw;
 }
 
+// The same prologue as a persistent grid (a few CTAs per SM) striding over the
+// tokens: each CTA issues the loads of its next token before it reduces and
+// writes the current one, so twice the bytes are in flight per CTA, and the
+// two block-wide sums share one barrier per token (double-buffered slots).
+#ifndef DT_PROLOGUE_PERSISTENT
+#define DT_PROLOGUE_PERSISTENT 0
+#endif
+__global__ void __launch_bounds__(kPrologueThreads, DT_PROLOGUE_PERSISTENT > 0 ? DT_PROLOGUE_PERSISTENT : 1)
+qk_norm_rope_loop_kernel(const PrologueParams p, long long M) {
+    __shared__ float red[2][2][kPrologueThreads / 32];  // [slot][q, k][warp]
+    const int h = threadIdx.x >> 4;
+    const int j = threadIdx.x & 15;
+    const int w = threadIdx.x >> 5;
+    const int d_lo = h * kHeadDim + 4 * j;
+    const int d_hi = d_lo + 64;
+    const float4 gq_lo = *reinterpret_cast<const float4*>(p.q_gain + d_lo);
+    const float4 gq_hi = *reinterpret_cast<const float4*>(p.q_gain + d_hi);
+    const float4 gk_lo = *reinterpret_cast<const float4*>(p.k_gain + d_lo);
+    const float4 gk_hi = *reinterpret_cast<const float4*>(p.k_gain + d_hi);
+    long long row = blockIdx.x;
+    if (row >= M) return;
+    float4 cur[6], nxt[6];
+    auto load = [&](long long r, float4 (&x)[6]) {
+        const float* qr = p.q + r * p.ld_in;
+        const float* kr = p.k + r * p.ld_in;
+        const float* vr = p.v + r * p.ld_in;
+        x[0] = *reinterpret_cast<const float4*>(qr + d_lo);
+        x[1] = *reinterpret_cast<const float4*>(qr + d_hi);
+        x[2] = *reinterpret_cast<const float4*>(kr + d_lo);
+        x[3] = *reinterpret_cast<const float4*>(kr + d_hi);
+        x[4] = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x);
+        x[5] = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x + 4);
+    };
+    auto sq4 = [](float4 a) { return a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w; };
+    load(row, cur);
+    for (int slot = 0;; slot ^= 1) {
+        const long long next = row + gridDim.x;
+        if (next < M) load(next, nxt);
+        float sq = sq4(cur[0]) + sq4(cur[1]);
+        float sk = sq4(cur[2]) + sq4(cur[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        if ((threadIdx.x & 31) == 0) {
+            red[slot][0][w] = sq;
+            red[slot][1][w] = sk;
+        }
+        __syncthreads();
+        sq = 0.f;
+        sk = 0.f;
+#pragma unroll
+        for (int i = 0; i < kPrologueThreads / 32; ++i) {
+            sq += red[slot][0][i];
+            sk += red[slot][1][i];
+        }
+        const float rq = sqrtf(sq / (float)kDModel + p.eps);
+        const float rk = sqrtf(sk / (float)kDModel + p.eps);
+        const int t = static_cast<int>(row % p.T);
+        const float* cs = p.cos_t + (long long)t * kHeadDim + 4 * j;
+        const float* sn = p.sin_t + (long long)t * kHeadDim + 4 * j;
+        const float4 c_lo = *reinterpret_cast<const float4*>(cs);
+        const float4 c_hi = *reinterpret_cast<const float4*>(cs + 64);
+        const float4 s_lo = *reinterpret_cast<const float4*>(sn);
+        const float4 s_hi = *reinterpret_cast<const float4*>(sn + 64);
+        auto rot = [&](float4 a, float4 b, float r, float4 ga, float4 gb, __nv_bfloat16* out) {
+            const float a0 = a.x / r * ga.x, a1 = a.y / r * ga.y, a2 = a.z / r * ga.z, a3 = a.w / r * ga.w;
+            const float b0 = b.x / r * gb.x, b1 = b.y / r * gb.y, b2 = b.z / r * gb.z, b3 = b.w / r * gb.w;
+            uint2 lo, hi;
+            lo.x = pack_bf16x2(a0 * c_lo.x - b0 * s_lo.x, a1 * c_lo.y - b1 * s_lo.y);
+            lo.y = pack_bf16x2(a2 * c_lo.z - b2 * s_lo.z, a3 * c_lo.w - b3 * s_lo.w);
+            hi.x = pack_bf16x2(b0 * c_hi.x + a0 * s_hi.x, b1 * c_hi.y + a1 * s_hi.y);
+            hi.y = pack_bf16x2(b2 * c_hi.z + a2 * s_hi.z, b3 * c_hi.w + a3 * s_hi.w);
+            *reinterpret_cast<uint2*>(out + row * kDModel + d_lo) = lo;
+            *reinterpret_cast<uint2*>(out + row * kDModel + d_hi) = hi;
+        };
+        rot(cur[0], cur[1], rq, gq_lo, gq_hi, p.qo);
+        rot(cur[2], cur[3], rk, gk_lo, gk_hi, p.ko);
+        *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) =
+            make_uint4(pack_bf16x2(cur[4].x, cur[4].y), pack_bf16x2(cur[4].z, cur[4].w),
+                       pack_bf16x2(cur[5].x, cur[5].y), pack_bf16x2(cur[5].z, cur[5].w));
+        if (next >= M) break;
+        row = next;
+#pragma unroll
+        for (int i = 0; i < 6; ++i) cur[i] = nxt[i];
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Head-sharded prologue (heads split over ranks, column-parallel QKV).  The
 // QK-RMSNorm sums squares over all 2048 columns of a token, i.e. over every
