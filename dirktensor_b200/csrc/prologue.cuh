@@ -44,16 +44,25 @@ struct Cast3 {
     const float4* src[3];
     uint2* dst[3];
 };
+// Each thread keeps kCastUnroll independent 16-byte loads in flight per iteration
+// (one at a time left a short cast latency-bound: 96 MB moved at ~74 % of the copy rate).
+constexpr int kCastUnroll = 4;
 __global__ void cast3_f32_bf16_kernel(Cast3 a, long long n4) {
     const float4* __restrict__ src = a.src[blockIdx.y];
     uint2* __restrict__ dst = a.dst[blockIdx.y];
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
-         i += (long long)gridDim.x * blockDim.x) {
-        const float4 v = src[i];
-        uint2 w;
-        w.x = pack_bf16x2(v.x, v.y);
-        w.y = pack_bf16x2(v.z, v.w);
-        dst[i] = w;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; i0 < n4; i0 += kCastUnroll * stride) {
+        float4 v[kCastUnroll];
+#pragma unroll
+        for (int u = 0; u < kCastUnroll; ++u) {
+            const long long i = i0 + u * stride;
+            if (i < n4) v[u] = src[i];
+        }
+#pragma unroll
+        for (int u = 0; u < kCastUnroll; ++u) {
+            const long long i = i0 + u * stride;
+            if (i < n4) dst[i] = make_uint2(pack_bf16x2(v[u].x, v[u].y), pack_bf16x2(v[u].z, v[u].w));
+        }
     }
 }
 
