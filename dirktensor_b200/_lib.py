@@ -98,6 +98,7 @@ SIGNATURES = {
                                         _P]),
     "dt_flash_fwd_qf32_exchange": (_I, [_P, _P, _P, ctypes.POINTER(_P), _I, _I, _LL, _P, _P, _I, _I, _I, _I, _F, _I,
                                         _P]),
+    "dt_exchange_barrier": (_I, [ctypes.POINTER(_P), _I, _I, ctypes.c_uint, _P]),
     "dt_ipc_get_handle": (_I, [_P, _P, ctypes.POINTER(_SZ)]),
     "dt_ipc_open": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
     "dt_ipc_close": (_I, [_P, _SZ]),

@@ -754,14 +754,14 @@ struct ShardState {
     dt_comm* comm = nullptr;
     int exchange = 0;  // 0: attention kernel stores into the owners' buffers (IPC), 1: NCCL all-to-all
     int h0 = 0, heads = 16;
-    // exchange 0: two receive buffers [G, M/G, w] bf16 (one per step parity) and every rank's
-    // mapping of them; rebuilt when M changes
+    // exchange 0: two receive buffers [G, M/G, w] bf16 (one per step parity) and the
+    // barrier's flag array (8 counters), and every rank's mapping of all three;
+    // rebuilt when M changes
     long long recv_tokens = 0;
-    void* recv[2] = {nullptr, nullptr};
-    void* peers[2][8] = {};
-    bool opened[2][8] = {};
-    float* barrier = nullptr;  // one float all-reduced after the stores
-    int step = 0;
+    void* recv[3] = {nullptr, nullptr, nullptr};
+    void* peers[3][8] = {};
+    bool opened[3][8] = {};
+    unsigned step = 0;
 };
 }  // namespace
 
@@ -1133,6 +1133,27 @@ int dt_flash_fwd_qf32_exchange(const float* q, const void* k, const void* v, voi
     DT_TRY(launch_flash(nullptr, k, v, nullptr, 1, (long long)H * D, softmax_m, softmax_l, nullptr, B, T, H, scale,
                         causal, st, sc, q));
     dt::elem::system_fence_kernel<<<1, 32, 0, st>>>();
+    DT_CUDA(cudaGetLastError());
+    return DT_OK;
+}
+
+int dt_exchange_barrier(void* const* flag_bufs, int ranks, int rank, unsigned epoch, void* stream) {
+    t_last_error.clear();
+    if (ranks < 1 || ranks > 8 || rank < 0 || rank >= ranks)
+        return fail(DT_ERR_INVALID_ARGUMENT, "ranks must be 1..8 and 0 <= rank < ranks");
+    if (!flag_bufs || epoch == 0) return fail(DT_ERR_INVALID_ARGUMENT, "need flag buffers and an epoch > 0");
+    dt::elem::BarrierArgs args{};
+    for (int r = 0; r < ranks; ++r) {
+        if (!flag_bufs[r] || ((uintptr_t)flag_bufs[r] & 3u))
+            return fail(DT_ERR_INVALID_ARGUMENT, "flag buffer %d must be non-null and 4-byte aligned", r);
+        args.flags[r] = static_cast<unsigned*>(flag_bufs[r]);
+    }
+    args.ranks = ranks;
+    args.rank = rank;
+    args.epoch = epoch;
+    int dev;
+    DT_TRY(prepare_device(&dev));
+    dt::elem::exchange_barrier_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(args);
     DT_CUDA(cudaGetLastError());
     return DT_OK;
 }
@@ -1543,11 +1564,10 @@ int dt_qk_norm_rope_shard(const float* q, const float* k, const float* v, long l
 static void shard_release(dt_attn* a) {
     ShardState* sh = a->shard;
     if (!sh) return;
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < 3; ++b)
         for (int r = 0; r < 8; ++r)
             if (sh->opened[b][r]) cudaIpcCloseMemHandle(sh->peers[b][r]);
-    for (int b = 0; b < 2; ++b) cudaFree(sh->recv[b]);
-    cudaFree(sh->barrier);
+    for (int b = 0; b < 3; ++b) cudaFree(sh->recv[b]);
     delete sh;
     a->shard = nullptr;
 }
@@ -1561,48 +1581,50 @@ static int shard_setup_exchange(dt_attn* a, long long M, cudaStream_t st) {
     NcclApi* n;
     DT_TRY(need_nccl(&n));
     DT_CUDA(cudaStreamSynchronize(st));
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < 3; ++b)
         for (int r = 0; r < 8; ++r)
             if (sh->opened[b][r]) {
                 DT_CUDA(cudaIpcCloseMemHandle(sh->peers[b][r]));
                 sh->opened[b][r] = false;
             }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 3; ++b) {
         DT_CUDA(cudaFree(sh->recv[b]));
         sh->recv[b] = nullptr;
     }
     sh->recv_tokens = 0;
     const size_t bytes = align256((size_t)M * sh->heads * 128 * 2);
     for (int b = 0; b < 2; ++b) DT_CUDA(cudaMalloc(&sh->recv[b], bytes));
+    DT_CUDA(cudaMalloc(&sh->recv[2], 256));
+    DT_CUDA(cudaMemset(sh->recv[2], 0, 256));
     const int G = c->world;
-    // my two handles -> device -> all-gather -> host
+    // my three handles -> device -> all-gather -> host
     constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
-    std::vector<uint8_t> mine(2 * kH), all((size_t)G * 2 * kH);
-    for (int b = 0; b < 2; ++b) {
+    std::vector<uint8_t> mine(3 * kH), all((size_t)G * 3 * kH);
+    for (int b = 0; b < 3; ++b) {
         cudaIpcMemHandle_t h;
         DT_CUDA(cudaIpcGetMemHandle(&h, sh->recv[b]));
         std::memcpy(mine.data() + b * kH, &h, kH);
     }
     uint8_t* dbuf = nullptr;
-    DT_CUDA(cudaMalloc(&dbuf, (size_t)(G + 1) * 2 * kH));
+    DT_CUDA(cudaMalloc(&dbuf, (size_t)(G + 1) * 3 * kH));
     int rc = DT_OK;
-    if (cudaMemcpy(dbuf, mine.data(), 2 * kH, cudaMemcpyHostToDevice) != cudaSuccess) rc = DT_ERR_CUDA;
+    if (cudaMemcpy(dbuf, mine.data(), 3 * kH, cudaMemcpyHostToDevice) != cudaSuccess) rc = DT_ERR_CUDA;
     if (rc == DT_OK)
-        rc = nccl_done(c, n->AllGather(dbuf, dbuf + 2 * kH, 2 * kH, ncclUint8, c->comm, st), "ncclAllGather(handles)");
+        rc = nccl_done(c, n->AllGather(dbuf, dbuf + 3 * kH, 3 * kH, ncclUint8, c->comm, st), "ncclAllGather(handles)");
     if (rc == DT_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = DT_ERR_CUDA;
-    if (rc == DT_OK && cudaMemcpy(all.data(), dbuf + 2 * kH, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess)
+    if (rc == DT_OK && cudaMemcpy(all.data(), dbuf + 3 * kH, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess)
         rc = DT_ERR_CUDA;
     cudaFree(dbuf);
     if (rc == DT_ERR_CUDA) return fail(DT_ERR_CUDA, "exchanging the receive-buffer handles failed");
     if (rc != DT_OK) return rc;
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < 3; ++b)
         for (int r = 0; r < G; ++r) {
             if (r == c->rank) {
                 sh->peers[b][r] = sh->recv[b];
                 continue;
             }
             cudaIpcMemHandle_t h;
-            std::memcpy(&h, all.data() + ((size_t)r * 2 + b) * kH, kH);
+            std::memcpy(&h, all.data() + ((size_t)r * 3 + b) * kH, kH);
             DT_CUDA(cudaIpcOpenMemHandle(&sh->peers[b][r], h, cudaIpcMemLazyEnablePeerAccess));
             sh->opened[b][r] = true;
         }
@@ -1650,7 +1672,7 @@ int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange
     float* stage = nullptr;
     if (cudaMalloc(&stage, 3 * wcols * d * 4) != cudaSuccess || cudaMalloc(&a->wqkv, 3 * wcols * d * 2) != cudaSuccess ||
         cudaMalloc(&a->wo, dd * 2) != cudaSuccess || cudaMalloc(&a->qg, d * 4) != cudaSuccess ||
-        cudaMalloc(&a->kg, d * 4) != cudaSuccess || cudaMalloc(&sh->barrier, 256) != cudaSuccess) {
+        cudaMalloc(&a->kg, d * 4) != cudaSuccess) {
         cudaFree(stage);
         return cleanup(fail(DT_ERR_OUT_OF_MEMORY, "cudaMalloc failed for the sharded layer's weights"));
     }
@@ -1668,8 +1690,7 @@ int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange
     if (rc == DT_OK && cudaDeviceSynchronize() != cudaSuccess) rc = fail(DT_ERR_CUDA, "weight cast failed");
     cudaFree(stage);
     if (rc == DT_OK && (cudaMemcpy(a->qg, w->q_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-                        cudaMemcpy(a->kg, w->k_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-                        cudaMemset(sh->barrier, 0, 256) != cudaSuccess))
+                        cudaMemcpy(a->kg, w->k_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess))
         rc = fail(DT_ERR_CUDA, "gain upload failed");
     if (rc == DT_OK) {
         const float *st, *ct;
@@ -1751,8 +1772,10 @@ int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int*
         DT_TRY(launch_flash(qb, kb, vb, o_local, 1, w, nullptr, nullptr, seq_lens, B, T, sh->heads, scale, 1, st));
         a_op = o_local;
     } else if (sh->exchange == 0) {
-        // attention stores each row into its owner's buffer; a one-float all-reduce after
-        // the system fence orders every rank's stores before the owners' projections
+        // attention stores each row into its owner's buffer; the flag barrier (a system
+        // fence, then every rank's step counter into every rank's flags over NVLink, and a
+        // bounded wait for all of them) orders every rank's stores before the owners'
+        // projections
         const int buf = sh->step & 1;
         sh->step++;
         Scatter sc;
@@ -1761,10 +1784,13 @@ int dt_attn_forward_sharded(dt_attn* a, const float* x, int B, int T, const int*
         sc.tokens_per_rank = tpr;
         sc.dst = sh->peers[buf];
         DT_TRY(launch_flash(qb, kb, vb, nullptr, 1, w, nullptr, nullptr, seq_lens, B, T, sh->heads, scale, 1, st, sc));
-        dt::elem::system_fence_kernel<<<1, 32, 0, st>>>();
+        dt::elem::BarrierArgs ba{};
+        for (int r = 0; r < G; ++r) ba.flags[r] = static_cast<unsigned*>(sh->peers[2][r]);
+        ba.ranks = G;
+        ba.rank = c->rank;
+        ba.epoch = sh->step;
+        dt::elem::exchange_barrier_kernel<<<1, 32, 0, st>>>(ba);
         DT_CUDA(cudaGetLastError());
-        DT_TRY(nccl_done(c, n->AllReduce(sh->barrier, sh->barrier, 1, ncclFloat32, ncclSum, c->comm, st),
-                         "ncclAllReduce(barrier)"));
         a_op = sh->recv[buf];
     } else {
         // local [M, w] token-major = [G, tpr, w]: slice g goes to rank g, plane g of mine comes from rank g

@@ -39,6 +39,46 @@ __global__ void system_fence_kernel() {
     if (threadIdx.x == 0) __threadfence_system();
 }
 
+// Barrier of the in-kernel exchange, on every rank after the kernel that stored
+// this rank's output rows into the owners' receive buffers: a system-scope
+// fence (the stream has ordered that kernel's stores before this one), then
+// thread r publishes `epoch` in rank r's flag array at slot `rank` (a release
+// store through the peer mapping) and waits until rank r's epoch has arrived
+// in this rank's own array (acquire loads).  The wait gives up after 1 second:
+// it records the site in the device error word and returns, so a rank that
+// never arrives cannot hang the GPU.  One thread per rank, ranks on different
+// GPUs; flags only grow (epochs count steps from 1).
+struct BarrierArgs {
+    unsigned* flags[8];  // flags[r]: rank r's flag array [8] as mapped in this process
+    int ranks;
+    int rank;
+    unsigned epoch;
+};
+__global__ void exchange_barrier_kernel(const BarrierArgs a) {
+    if (threadIdx.x == 0) __threadfence_system();
+    __syncthreads();
+    const int r = threadIdx.x;
+    if (r >= a.ranks) return;
+    const unsigned epoch = a.epoch;
+    unsigned* slot = a.flags[r] + a.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(epoch) : "memory");
+    const unsigned* mine = a.flags[a.rank] + r;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if ((int)(v - epoch) >= 0) break;
+        if ((it & 63u) == 63u) {
+            if (error_raised()) break;
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                report_error(kDevTimeoutBase | 0x90u, (unsigned)r);
+                break;
+            }
+        }
+        __nanosleep(64);
+    }
+}
+
 // Three tensors in one launch (raw Q, K, V); blockIdx.y selects the tensor.
 struct Cast3 {
     const float4* src[3];

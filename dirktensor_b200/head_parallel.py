@@ -18,8 +18,10 @@ Two exchange modes:
   fused (default): the flash kernel's epilogue
       stores each output row straight into the owning rank's receive buffer
       over NVLink (peer pointers from CUDA IPC, plain stores), i.e. attention and
-      exchange are one kernel; a one-element all-reduce on the same stream then
-      orders every rank's stores before the owners' O projections.  Receive
+      exchange are one kernel; a flag barrier kernel on the same stream (each
+      rank releases a step counter into every rank's flag array over NVLink and
+      waits, bounded, for all of them) then orders every rank's stores before
+      the owners' O projections.  Receive
       buffers are double-buffered across steps, so a rank that runs ahead never
       overwrites a buffer its owner is still projecting.  Rows leave through
       shared memory so that each warp stores two whole 256-byte rows per
@@ -160,22 +162,25 @@ class HeadParallelAttention:
         self.close()
         L = lib()
         recv = [torch.empty(shape, dtype=torch.bfloat16, device=device) for _ in range(2)]
-        mine = torch.zeros((2, 72), dtype=torch.uint8)
-        for i, buf in enumerate(recv):
+        # the barrier's flag array (8 counters) travels with the receive buffers
+        flags = torch.zeros(64, dtype=torch.int32, device=device)
+        bufs = recv + [flags]
+        mine = torch.zeros((3, 72), dtype=torch.uint8)
+        for i, buf in enumerate(bufs):
             h = (ctypes.c_uint8 * 64)()
             off = ctypes.c_size_t()
             check(L.dt_ipc_get_handle(buf.data_ptr(), h, ctypes.byref(off)))
             mine[i, :64] = torch.tensor(list(bytes(h)), dtype=torch.uint8)
             mine[i, 64:] = torch.tensor(list(off.value.to_bytes(8, "little")), dtype=torch.uint8)
-        allh = torch.empty((G, 2, 72), dtype=torch.uint8, device=device)
+        allh = torch.empty((G * 3, 72), dtype=torch.uint8, device=device)
         dist.all_gather_into_tensor(allh, mine.to(device), group=self.group)
-        allh = allh.cpu()
+        allh = allh.view(G, 3, 72).cpu()
         ptrs, opened = [], []
-        for i in range(2):
+        for i in range(3):
             arr = (ctypes.c_void_p * G)()
             for r in range(G):
                 if r == self.rank:
-                    arr[r] = recv[i].data_ptr()
+                    arr[r] = bufs[i].data_ptr()
                     continue
                 hb = bytes(allh[r, i, :64].tolist())
                 off = int.from_bytes(bytes(allh[r, i, 64:].tolist()), "little")
@@ -184,8 +189,7 @@ class HeadParallelAttention:
                 arr[r] = p.value
                 opened.append((p.value, off))
             ptrs.append(arr)
-        self._fused = (shape, recv, ptrs, opened)
-        self._barrier = torch.zeros(1, dtype=torch.float32, device=device)
+        self._fused = (shape, recv, ptrs, opened, flags)
 
     def close(self):
         """Unmaps the peers' receive buffers (fused exchange)."""
@@ -212,8 +216,9 @@ class HeadParallelAttention:
                                                torch.cuda.current_stream(q.device).cuda_stream))
         if events is not None:
             events[1].record()
-        # stream-ordered barrier: every rank's stores into my buffer precede my projection
-        dist.all_reduce(self._barrier, group=self.group)
+        # every rank's stores into my buffer precede my projection: flag barrier on the GPU
+        check(lib().dt_exchange_barrier(self._fused[2][2], self.world, self.rank, self._step,
+                                        torch.cuda.current_stream(q.device).cuda_stream))
         return self._fused[1][buf]
 
     def forward(self, q, k, v, scale: float, causal: bool = True, events=None,
@@ -315,7 +320,7 @@ class HeadParallelAttentionLayer(HeadParallelAttention):
             self._step += 1
             check(lib().dt_flash_fwd_bf16_exchange(qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), self._fused[2][buf],
                                                    G, self.rank, M // G, None, None, B, T, Hl, D, scale, 1, stream))
-            dist.all_reduce(self._barrier, group=self.group)
+            check(lib().dt_exchange_barrier(self._fused[2][2], G, self.rank, self._step, stream))
             return self._fused[1][buf]
         out = self._buf("o_local", (M, Hl * D), torch.bfloat16, qb.device)
         check(lib().dt_flash_fwd_bf16(qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), out.data_ptr(), 1, Hl * D, None,

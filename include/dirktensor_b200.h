@@ -107,6 +107,17 @@ int dt_flash_bwd_host(const float* dout, const float* out, const float* softmax_
 int dt_flash_fwd_noalloc(const float* q, const float* k, const float* v, float* o, float* softmax_m,
                          float* softmax_l, int B, int T, int H, int D, float scale, int causal, void* stream);
 
+/* Barrier of the in-kernel exchange (no counterpart in the reference, whose
+ * heads share one process): after dt_flash_fwd_*_exchange on every rank, each
+ * rank publishes `epoch` (a per-step counter starting at 1) into every rank's
+ * flag array and waits, on the GPU, until every rank's epoch has arrived in its
+ * own.  flag_bufs[r]: rank r's array of 8 uint32 (zero-initialised device
+ * memory, mapped into this process, e.g. with dt_ipc_open; flag_bufs[rank] is
+ * this rank's own).  The wait gives up after 1 second and records
+ * DT_ERR_DEVICE_TIMEOUT (see dt_check_device_error).  Asynchronous on `stream`;
+ * the O projection that reads the receive buffer goes after it. */
+int dt_exchange_barrier(void* const* flag_bufs, int ranks, int rank, unsigned epoch, void* stream);
+
 /* Packed-operand form used inside the layer and by head-sharded callers:
  * q, k, v are bf16 [B, T, H, D] device arrays; o is fp32 (o_bf16 = 0) or
  * bf16 (o_bf16 = 1) with o_row_stride elements between consecutive tokens
