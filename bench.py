@@ -376,9 +376,9 @@ def main():
                          "ms_per_launch": ms_flash, "flops_per_launch": f_flash_rank, "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            # one K+V cast launch + flash (which rounds fp32 Q itself) + O projection; the fused
-            # exchange adds its one-thread system fence
-            "gpu_launches": (4 if world > 1 and args.exchange == "fused" else 3) * args.steps,
+            # one K+V cast launch + attention (which rounds fp32 Q itself) + O projection; the fused
+            # exchange adds its one-thread system fence and the flag barrier kernel
+            "gpu_launches": (5 if world > 1 and args.exchange == "fused" else 3) * args.steps,
             "clocks": clocks,
             "config1_t4096": t4096,
             "exchange_variants": variants,
