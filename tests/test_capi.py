@@ -109,3 +109,32 @@ def test_rope_tables_equal_oracle():
     s, c = dt.rope_tables(8192, 128, 500000.0)
     os_, oc = oracle.rope_tables(8192, 128, 500000.0)
     assert np.array_equal(s, os_) and np.array_equal(c, oc)
+
+
+def test_head_parallel_entry_points_validate_before_any_device_work():
+    """The communicator, sharded-layer, barrier and sharded-prologue entry points
+    reject bad arguments (world size, ranks, sizes, null handles) before they
+    touch a device or NCCL."""
+    L = _lib.lib()
+    uid = (ctypes.c_uint8 * 128)()
+    comm = ctypes.c_void_p()
+    assert L.dt_comm_create(uid, 9, 0, 0, 1000, ctypes.byref(comm)) == 1      # world > 8
+    assert L.dt_comm_create(uid, 2, 2, 0, 1000, ctypes.byref(comm)) == 1      # rank out of range
+    assert L.dt_comm_create(uid, 2, 0, 0, 0, ctypes.byref(comm)) == 1         # no timeout
+    assert L.dt_comm_destroy(None) == 0 and L.dt_comm_abort(None) == 0
+    attn = ctypes.c_void_p()
+    w = _lib.dt_attn_weights()
+    assert L.dt_attn_create_sharded(ctypes.byref(w), None, 0, ctypes.byref(attn)) == 1
+    assert L.dt_attn_forward_sharded(None, None, 1, 512, None, 0, None, None) == 1
+    assert L.dt_attn_forward_sharded_host(None, None, 1, 512, None, 0, None) == 1
+    flags = (ctypes.c_void_p * 2)(16, 16)
+    assert L.dt_exchange_barrier(flags, 9, 0, 1, None) == 1                   # ranks > 8
+    assert L.dt_exchange_barrier(flags, 2, 0, 0, None) == 1                   # epoch 0
+    assert L.dt_exchange_barrier((ctypes.c_void_p * 2)(16, None), 2, 0, 1, None) == 1
+    assert b"flag buffer" in L.dt_last_error()
+    assert L.dt_qk_sumsq(None, None, 2048, 6, 4, None, None) == 1            # width % 4
+    assert L.dt_qk_sumsq(None, None, 2048, 256, 0, None, None) == 0          # empty: no-op
+    st = L.dt_qk_norm_rope_shard(None, None, None, 768, None, None, None, 3, None, None, None, 1, 4, 1e-6, 5e5, None)
+    assert st == 1 and b"heads" in L.dt_last_error()
+    assert L.dt_cast2_f32_bf16(None, None, None, None, 6, None) == 1
+    assert L.dt_cast2_f32_bf16(None, None, None, None, 0, None) == 0
