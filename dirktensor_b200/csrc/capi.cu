@@ -1668,9 +1668,11 @@ int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange
         t_last_error = msg;
         return code;
     };
-    // [Wq_r; Wk_r; Wv_r]: this rank's head rows of each projection, then all of Wo
+    // [Wq_r; Wk_r; Wv_r]: this rank's head rows of each projection, then all of Wo, staged
+    // in fp32 one after the other in a buffer that holds the larger of the two
     float* stage = nullptr;
-    if (cudaMalloc(&stage, 3 * wcols * d * 4) != cudaSuccess || cudaMalloc(&a->wqkv, 3 * wcols * d * 2) != cudaSuccess ||
+    const size_t stage_floats = std::max(3 * wcols * d, dd);
+    if (cudaMalloc(&stage, stage_floats * 4) != cudaSuccess || cudaMalloc(&a->wqkv, 3 * wcols * d * 2) != cudaSuccess ||
         cudaMalloc(&a->wo, dd * 2) != cudaSuccess || cudaMalloc(&a->qg, d * 4) != cudaSuccess ||
         cudaMalloc(&a->kg, d * 4) != cudaSuccess) {
         cudaFree(stage);
@@ -1678,20 +1680,23 @@ int dt_attn_create_sharded(const dt_attn_weights* w, dt_comm* comm, int exchange
     }
     const float* src[3] = {w->q_proj, w->k_proj, w->v_proj};
     int rc = DT_OK;
-    for (int i = 0; i < 3 && rc == DT_OK; ++i)
-        if (cudaMemcpy(stage + i * wcols * d, src[i] + (size_t)sh->h0 * 128 * d, wcols * d * 4,
-                       cudaMemcpyHostToDevice) != cudaSuccess)
-            rc = fail(DT_ERR_CUDA, "weight upload failed");
+    cudaError_t ce = cudaSuccess;
+    for (int i = 0; i < 3 && ce == cudaSuccess; ++i)
+        ce = cudaMemcpy(stage + i * wcols * d, src[i] + (size_t)sh->h0 * 128 * d, wcols * d * 4,
+                        cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) rc = fail(DT_ERR_CUDA, "weight upload failed: %s", cudaGetErrorString(ce));
     if (rc == DT_OK) rc = launch_cast(stage, a->wqkv, (long long)(3 * wcols * d), nullptr);
-    if (rc == DT_OK && cudaDeviceSynchronize() != cudaSuccess) rc = fail(DT_ERR_CUDA, "weight cast failed");
-    if (rc == DT_OK && cudaMemcpy(stage, w->o_proj, dd * 4, cudaMemcpyHostToDevice) != cudaSuccess)
-        rc = fail(DT_ERR_CUDA, "weight upload failed");
+    if (rc == DT_OK && (ce = cudaDeviceSynchronize()) != cudaSuccess)
+        rc = fail(DT_ERR_CUDA, "weight cast failed: %s", cudaGetErrorString(ce));
+    if (rc == DT_OK && (ce = cudaMemcpy(stage, w->o_proj, dd * 4, cudaMemcpyHostToDevice)) != cudaSuccess)
+        rc = fail(DT_ERR_CUDA, "weight upload failed: %s", cudaGetErrorString(ce));
     if (rc == DT_OK) rc = launch_cast(stage, a->wo, (long long)dd, nullptr);
-    if (rc == DT_OK && cudaDeviceSynchronize() != cudaSuccess) rc = fail(DT_ERR_CUDA, "weight cast failed");
+    if (rc == DT_OK && (ce = cudaDeviceSynchronize()) != cudaSuccess)
+        rc = fail(DT_ERR_CUDA, "weight cast failed: %s", cudaGetErrorString(ce));
     cudaFree(stage);
-    if (rc == DT_OK && (cudaMemcpy(a->qg, w->q_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-                        cudaMemcpy(a->kg, w->k_norm, d * 4, cudaMemcpyHostToDevice) != cudaSuccess))
-        rc = fail(DT_ERR_CUDA, "gain upload failed");
+    if (rc == DT_OK && ((ce = cudaMemcpy(a->qg, w->q_norm, d * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+                        (ce = cudaMemcpy(a->kg, w->k_norm, d * 4, cudaMemcpyHostToDevice)) != cudaSuccess))
+        rc = fail(DT_ERR_CUDA, "gain upload failed: %s", cudaGetErrorString(ce));
     if (rc == DT_OK) {
         const float *st, *ct;
         rc = ensure_rope(dev, a->theta, &st, &ct);
