@@ -467,9 +467,11 @@ int launch_flash_bwd(const void* qb, const void* kb, const void* vb, const float
 
 // seq_lens/seq_T (optional): right-padded batch; output tiles entirely in a
 // sequence's padding are skipped (and written as zeros when pad_zero).
+// split_c2 / split_ldc2 / split_col0: columns >= split_col0 go to split_c2 as bf16 (kStore only).
 int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N, int K, long long ldc,
                 cudaStream_t st, int a_planes = 1, int epilogue = dt::gemm::kStore, const int* seq_lens = nullptr,
-                int seq_T = 0, int pad_zero = 0, int a_mn = 0, int b_mn = 0) {
+                int seq_T = 0, int pad_zero = 0, int a_mn = 0, int b_mn = 0, void* split_c2 = nullptr,
+                long long split_ldc2 = 0, int split_col0 = 0) {
     if (M == 0 || N == 0) return DT_OK;
     CUtensorMap ma, mb;
     const int plane_k = K / a_planes;
@@ -504,6 +506,13 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
     p.epilogue = epilogue;
     p.a_mn = a_mn;
     p.b_mn = b_mn;
+    if (split_c2) {
+        if (epilogue != dt::gemm::kStore || c_bf16 || (split_col0 % 32) != 0)
+            return fail(DT_ERR_INVALID_ARGUMENT, "split output needs an fp32 store epilogue and a column multiple of 32");
+        p.C2 = split_c2;
+        p.ldc2 = split_ldc2;
+        p.c2_col0 = split_col0;
+    }
     // tiles are 256 rows on SM pairs, 128 on one SM: skip only if they never straddle sequences
     const int tile_rows = pair ? dt::gemm2::kBM : dt::gemm::kBM;
     if (seq_lens && seq_T > 0 && (seq_T % tile_rows) == 0) {
@@ -1927,9 +1936,11 @@ static int attn_core(dt_attn* a, const void* xb, int B, int T, const int* seq_le
     float* sm_l = reinterpret_cast<float*>(rest + 4 * act + align256(M * a->n_heads * 4));
     const float *sin_t, *cos_t;
     DT_TRY(ensure_rope(dev, a->theta, &sin_t, &cos_t));
-    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st, 1, dt::gemm::kStore, seq_lens, T,
-                       0));                                                         // [q|k|v] = x Wqkv^T
-    DT_TRY(launch_prologue(qkv, qkv + d, qkv + 2 * d, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
+    // [q|k|v] = x Wqkv^T: q and k in fp32 (the norm's input, kept for the backward), v
+    // straight in bf16 (attention's operand; the prologue leaves it alone)
+    DT_TRY(launch_gemm(xb, a->wqkv, qkv, 0, (int)M, 3 * d, d, 3 * d, st, 1, dt::gemm::kStore, seq_lens, T, 0, 0, 0,
+                       vb, d, 2 * d));
+    DT_TRY(launch_prologue(qkv, qkv + d, nullptr, 3 * d, a->qg, a->kg, sin_t, cos_t, qb, kb, vb, B, T, a->eps,
                            st));                                                    // norm + RoPE
     DT_TRY(launch_flash(qb, kb, vb, ab, 1, d, sm_m, sm_l, seq_lens, B, T, a->n_heads, 1.0f / std::sqrt(128.0f), 1,
                         st));                                                       // attention

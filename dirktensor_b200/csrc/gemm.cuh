@@ -72,6 +72,12 @@ struct Params {
     int b_mn;           // 1: B stored [K, N] row-major (N contiguous)
     int tiles_m;        // ceil(M / tile rows)
     int m_fastest;      // tile order: 0 = N varies fastest, 1 = M varies fastest
+    // Split output (optional, C2 != null): columns >= c2_col0 (a multiple of 32) go
+    // to C2 as bf16, [M, ldc2] row-major from column c2_col0 on; the rest to C.
+    // The QKV projection writes q and k in fp32 for the norm and v straight in bf16.
+    void* C2;
+    long long ldc2;
+    int c2_col0;
 };
 
 // Tile t's (row-tile, column-tile) in the persistent walk.  The order keeps the
@@ -109,6 +115,21 @@ enum : unsigned { kSiteEmpty = 0x21, kSiteFull, kSiteAcc, kSiteDone, kSiteAccEmp
 
 __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, const float (&v)[32]) {
     if (row >= p.M || col >= p.N) return;
+    if (p.C2 != nullptr && col >= p.c2_col0) {
+        __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.C2) + (long long)row * p.ldc2 + (col - p.c2_col0);
+        if (col + 32 <= p.N) {
+            uint4* d = reinterpret_cast<uint4*>(base);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                d[i] = make_uint4(pack_bf16x2(v[8 * i + 0], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                                  pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+        } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+                if (col + e < p.N) base[e] = __float2bfloat16_rn(v[e]);
+        }
+        return;
+    }
     if (col + 32 <= p.N) {
         if (p.c_bf16) {
             uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)row * p.ldc + col);

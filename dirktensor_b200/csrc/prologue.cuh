@@ -113,7 +113,7 @@ constexpr int kPrologueThreads = 256;
 struct PrologueParams {
     const float* q;       // [M, ld_in] rows of the projection output (q part)
     const float* k;
-    const float* v;
+    const float* v;       // null: v is not converted (written in bf16 by the projection)
     long long ld_in;      // elements between consecutive tokens
     const float* q_gain;  // [2048]
     const float* k_gain;  // [2048]
@@ -155,9 +155,13 @@ qk_norm_rope_kernel(const PrologueParams p) {
     const float4 qb = *reinterpret_cast<const float4*>(qr + d_hi);
     const float4 ka = *reinterpret_cast<const float4*>(kr + d_lo);
     const float4 kb = *reinterpret_cast<const float4*>(kr + d_hi);
-    // v: this thread converts 8 consecutive elements
-    const float4 va = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x);
-    const float4 vb = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x + 4);
+    // v: this thread converts 8 consecutive elements (v == null: the producer
+    // already wrote v in bf16 and the prologue leaves it alone)
+    float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+    if (p.v) {
+        va = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x);
+        vb = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x + 4);
+    }
 
     float sq = qa.x * qa.x + qa.y * qa.y + qa.z * qa.z + qa.w * qa.w + qb.x * qb.x + qb.y * qb.y + qb.z * qb.z +
                qb.w * qb.w;
@@ -194,12 +198,14 @@ qk_norm_rope_kernel(const PrologueParams p) {
     rot(qa, qb, rq, gq_lo, gq_hi, p.qo);
     rot(ka, kb, rk, gk_lo, gk_hi, p.ko);
 
-    uint4 vw;
-    vw.x = pack_bf16x2(va.x, va.y);
-    vw.y = pack_bf16x2(va.z, va.w);
-    vw.z = pack_bf16x2(vb.x, vb.y);
-    vw.w = pack_bf16x2(vb.z, vb.w);
-    *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) = vw;
+    if (p.v) {
+        uint4 vw;
+        vw.x = pack_bf16x2(va.x, va.y);
+        vw.y = pack_bf16x2(va.z, va.w);
+        vw.z = pack_bf16x2(vb.x, vb.y);
+        vw.w = pack_bf16x2(vb.z, vb.w);
+        *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) = vw;
+    }
 }
 
 // The same prologue as a persistent grid (a few CTAs per SM) striding over the
@@ -232,8 +238,10 @@ qk_norm_rope_loop_kernel(const PrologueParams p, long long M) {
         x[1] = *reinterpret_cast<const float4*>(qr + d_hi);
         x[2] = *reinterpret_cast<const float4*>(kr + d_lo);
         x[3] = *reinterpret_cast<const float4*>(kr + d_hi);
-        x[4] = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x);
-        x[5] = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x + 4);
+        if (p.v) {
+            x[4] = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x);
+            x[5] = *reinterpret_cast<const float4*>(vr + 8 * threadIdx.x + 4);
+        }
     };
     auto sq4 = [](float4 a) { return a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w; };
     load(row, cur);
@@ -281,9 +289,10 @@ qk_norm_rope_loop_kernel(const PrologueParams p, long long M) {
         };
         rot(cur[0], cur[1], rq, gq_lo, gq_hi, p.qo);
         rot(cur[2], cur[3], rk, gk_lo, gk_hi, p.ko);
-        *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) =
-            make_uint4(pack_bf16x2(cur[4].x, cur[4].y), pack_bf16x2(cur[4].z, cur[4].w),
-                       pack_bf16x2(cur[5].x, cur[5].y), pack_bf16x2(cur[5].z, cur[5].w));
+        if (p.v)
+            *reinterpret_cast<uint4*>(p.vo + row * kDModel + 8 * threadIdx.x) =
+                make_uint4(pack_bf16x2(cur[4].x, cur[4].y), pack_bf16x2(cur[4].z, cur[4].w),
+                           pack_bf16x2(cur[5].x, cur[5].y), pack_bf16x2(cur[5].z, cur[5].w));
         if (next >= M) break;
         row = next;
 #pragma unroll
