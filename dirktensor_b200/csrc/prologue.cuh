@@ -213,7 +213,7 @@ qk_norm_rope_kernel(const PrologueParams p) {
 // writes the current one, so twice the bytes are in flight per CTA, and the
 // two block-wide sums share one barrier per token (double-buffered slots).
 #ifndef DT_PROLOGUE_PERSISTENT
-#define DT_PROLOGUE_PERSISTENT 0
+#define DT_PROLOGUE_PERSISTENT 2
 #endif
 __global__ void __launch_bounds__(kPrologueThreads, DT_PROLOGUE_PERSISTENT > 0 ? DT_PROLOGUE_PERSISTENT : 1)
 qk_norm_rope_loop_kernel(const PrologueParams p, long long M) {
