@@ -859,7 +859,7 @@ def bench_prologue(torch, dt, dev, args):
     nbytes = Mt * 3 * DM * (4 + 2)
     peaks, src = load_peaks()
     hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-    return {"kernel": "qk_norm_rope_kernel", "tokens": Mt, "ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+    return {"kernel": "qk_norm_rope_loop_kernel", "tokens": Mt, "ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
             "peak_gbs": hbm, "frac_hbm": nbytes / ms / 1e6 / hbm, "peak_source": f"{src} HBM copy"}
 
 
