@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
+#include <utility>
 #include <mutex>
 #include <thread>
 #include <string>
@@ -209,6 +210,36 @@ private:
     bool restore_ = false;
 };
 
+// Programmatic dependent launch (PDL) for the kernels that begin with pdl_enter()
+// (the cast, both GEMMs, the prologue and the attention kernel): launched with the
+// programmatic-serialization attribute, a kernel's CTAs may be dispatched while the
+// previous kernel on the stream finishes; they wait in pdl_enter() until it has
+// completed, before any global memory access.  0 launches them plainly.
+#ifndef DT_PDL
+#define DT_PDL 1
+#endif
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+#if DT_PDL
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DT_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+#else
+    kernel<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+    DT_CUDA(cudaGetLastError());
+#endif
+    return DT_OK;
+}
+
 int current_device(int* dev) {
     DT_CUDA(cudaGetDevice(dev));
     if (*dev < 0 || *dev >= 64) return fail(DT_ERR_UNSUPPORTED, "device index %d out of range", *dev);
@@ -314,10 +345,8 @@ int launch_cast(const float* src, void* dst, long long n, cudaStream_t st) {
     const int threads = 256;
     long long blocks = (n4 + threads - 1) / threads;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    dt::elem::cast_f32_bf16_kernel<<<(unsigned)blocks, threads, 0, st>>>(reinterpret_cast<const float4*>(src),
-                                                                         reinterpret_cast<uint2*>(dst), n4);
-    DT_CUDA(cudaGetLastError());
-    return DT_OK;
+    return launch_pdl(dt::elem::cast_f32_bf16_kernel, dim3((unsigned)blocks), dim3(threads), 0, st,
+                      reinterpret_cast<const float4*>(src), reinterpret_cast<uint2*>(dst), n4);
 }
 
 // Casts the first `count` (1..3) of a, b, c in one launch.
@@ -402,9 +431,8 @@ int launch_flash(const void* q, const void* k, const void* v, void* o, int o_bf1
     p.q_row_stride = (long long)H * 128;
     const long long grid = (long long)p.nblk * B * H;
     if (grid > 0x7fffffffLL) return fail(DT_ERR_INVALID_ARGUMENT, "problem too large (%lld CTAs)", grid);
-    dt::attn_fwd::attn_fwd_kernel<<<(unsigned)grid, dt::attn_fwd::kThreads, kFlashSmem, st>>>(mq, mk, mv, p);
-    DT_CUDA(cudaGetLastError());
-    return DT_OK;
+    return launch_pdl(dt::attn_fwd::attn_fwd_kernel, dim3((unsigned)grid), dim3(dt::attn_fwd::kThreads), kFlashSmem, st,
+                      mq, mk, mv, p);
 }
 
 // Attention backward on bf16 Q/K/V.  dout fp32 [B,T,H,D]; O fp32 (out) or bf16
@@ -538,17 +566,15 @@ int launch_gemm(const void* A, const void* Bm, void* C, int c_bf16, int M, int N
         p.tiles_m = (M + dt::gemm2::kBM - 1) / dt::gemm2::kBM;
         p.num_tiles = p.tiles_n * p.tiles_m;
         const int clusters = std::max(1, std::min(p.num_tiles, sms / 2));
-        dt::gemm2::gemm_bf16_tn_2sm_kernel<<<2 * clusters, dt::gemm2::kThreads, kGemm2Smem, st>>>(ma, mb, p);
-        DT_CUDA(cudaGetLastError());
-        return DT_OK;
+        return launch_pdl(dt::gemm2::gemm_bf16_tn_2sm_kernel, dim3(2 * clusters), dim3(dt::gemm2::kThreads),
+                          kGemm2Smem, st, ma, mb, p);
     }
     const int grid = (int)std::min<long long>(tiles, sms);  // persistent: one CTA per SM
     if (narrow)
-        dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kNarrowBN><<<grid, dt::gemm::kThreads, kGemmNarrowSmem, st>>>(ma, mb, p);
-    else
-        dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kBN><<<grid, dt::gemm::kThreads, kGemmSmem, st>>>(ma, mb, p);
-    DT_CUDA(cudaGetLastError());
-    return DT_OK;
+        return launch_pdl(dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kNarrowBN>, dim3(grid), dim3(dt::gemm::kThreads),
+                          kGemmNarrowSmem, st, ma, mb, p);
+    return launch_pdl(dt::gemm::gemm_bf16_tn_kernel<dt::gemm::kBN>, dim3(grid), dim3(dt::gemm::kThreads), kGemmSmem,
+                      st, ma, mb, p);
 }
 
 int launch_prologue(const float* q, const float* k, const float* v, long long ld_in, const float* qg,
@@ -577,13 +603,12 @@ int launch_prologue(const float* q, const float* k, const float* v, long long ld
         cudaGetDevice(&dev);
         const int sms = (dev >= 0 && dev < 64) ? g_dev[dev].num_sms : 148;
         const long long grid = std::min<long long>(M, (long long)sms * DT_PROLOGUE_PERSISTENT);
-        dt::elem::qk_norm_rope_loop_kernel<<<(unsigned)grid, dt::elem::kPrologueThreads, 0, st>>>(p, M);
+        return launch_pdl(dt::elem::qk_norm_rope_loop_kernel, dim3((unsigned)grid), dim3(dt::elem::kPrologueThreads), 0,
+                          st, p, M);
     }
 #else
-    dt::elem::qk_norm_rope_kernel<<<(unsigned)M, dt::elem::kPrologueThreads, 0, st>>>(p);
+    return launch_pdl(dt::elem::qk_norm_rope_kernel, dim3((unsigned)M), dim3(dt::elem::kPrologueThreads), 0, st, p);
 #endif
-    DT_CUDA(cudaGetLastError());
-    return DT_OK;
 }
 
 int launch_sumsq(const float* q, const float* k, long long ld, int width, long long M, float* ss, cudaStream_t st) {

@@ -345,6 +345,19 @@ __device__ __forceinline__ void regs_decrease() {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// Programmatic dependent launch.  Called first in the kernels that the layer path
+// launches with the programmatic-serialization attribute: `launch_dependents` lets the
+// next such kernel on the stream be scheduled once every CTA of this one has started,
+// and `wait` holds this CTA until the previous kernel on the stream has completed and
+// its memory is visible.  Every global access of the kernel comes after the wait, so
+// its results are those of a plain stream-ordered launch; the overlap is the
+// launch latency and CTA dispatch of the next kernel.  (Both are no-ops in a kernel
+// launched without the attribute.)
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -173,6 +173,7 @@ template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const Params p) {
+    pdl_enter();
     constexpr int kStages = Cfg<BN>::kStages;
     constexpr int kBBytes = Cfg<BN>::kBBytes;
     extern __shared__ uint8_t smem_raw[];

@@ -20,6 +20,7 @@ namespace elem {
 
 // n4: number of float4 groups; each thread handles float4 groups grid-stride.
 __global__ void cast_f32_bf16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst, long long n4) {
+    pdl_enter();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
          i += (long long)gridDim.x * blockDim.x) {
         const float4 v = src[i];
@@ -140,6 +141,7 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 
 __global__ void __launch_bounds__(kPrologueThreads)
 qk_norm_rope_kernel(const PrologueParams p) {
+    pdl_enter();
     __shared__ float red_q[8], red_k[8];
     const long long row = blockIdx.x;
     const int t = static_cast<int>(row % p.T);
@@ -217,6 +219,7 @@ qk_norm_rope_kernel(const PrologueParams p) {
 #endif
 __global__ void __launch_bounds__(kPrologueThreads, DT_PROLOGUE_PERSISTENT > 0 ? DT_PROLOGUE_PERSISTENT : 1)
 qk_norm_rope_loop_kernel(const PrologueParams p, long long M) {
+    pdl_enter();
     __shared__ float red[2][2][kPrologueThreads / 32];  // [slot][q, k][warp]
     const int h = threadIdx.x >> 4;
     const int j = threadIdx.x & 15;
