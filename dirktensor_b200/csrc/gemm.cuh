@@ -108,6 +108,7 @@ struct __align__(1024) SmemT {
     uint64_t acc_empty[kAccs];
     uint64_t mma_done;
     uint32_t tmem_base;
+    alignas(128) float stage[4][32 * 32];  // epilogue: one 32 x 32 fp32 block per epilogue warp
 };
 using Smem = SmemT<kBN>;
 
@@ -167,6 +168,41 @@ __device__ __forceinline__ void store_chunk(const Params& p, int row, int col, c
             }
         }
     }
+}
+
+// True when the fp32 columns [col, col + 32) leave through store_rows_f32_staged
+// (warp-uniform: depends on the column and the parameters only).
+__device__ __forceinline__ bool staged_f32(const Params& p, int col) {
+    return p.epilogue == kStore && !p.c_bf16 && (p.C2 == nullptr || col < p.c2_col0) && col + 32 <= p.N;
+}
+
+// Coalesced store of a warp's 32 rows x 32 fp32 columns (lane i holds row row0 + i).
+// The block passes through this warp's 4 KB of shared memory -- 16-byte chunk j of
+// row r at position j ^ (r & 7), so that both the row-wise writes and the
+// column-wise reads spread over all banks -- and each store instruction then
+// writes four whole 128-byte row segments instead of 32 scattered 16-byte pieces.
+// Rows >= M are skipped.
+__device__ __forceinline__ void store_rows_f32_staged(const Params& p, uint32_t stage, int row0, int col,
+                                                      const float (&v)[32], int lane) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(stage + (uint32_t)lane * 128 +
+                                                                      ((uint32_t)(j ^ (lane & 7)) << 4)),
+                     "f"(v[4 * j]), "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                     : "memory");
+    __syncwarp();
+    const int j = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = 4 * i + (lane >> 3);
+        float4 x;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                     : "r"(stage + (uint32_t)r * 128 + ((uint32_t)(j ^ (r & 7)) << 4)));
+        if (row0 + r < p.M)
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + (long long)(row0 + r) * p.ldc + col + 4 * j) = x;
+    }
+    __syncwarp();  // the next block reuses the stage
 }
 
 template <int BN>
@@ -332,12 +368,16 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                     }
                 }
             } else {
+                const uint32_t stage = smem_u32(sm.stage[q]);
 #pragma unroll 1
                 for (int cc = 0; cc < BN / 32; ++cc) {
                     float v[32];
                     tmem_ld32(taddr + cc * 32, v);
                     tmem_wait_ld();
-                    store_chunk(p, row, n0 + cc * 32, v);
+                    if (staged_f32(p, n0 + cc * 32))
+                        store_rows_f32_staged(p, stage, row - lane, n0 + cc * 32, v, lane);
+                    else
+                        store_chunk(p, row, n0 + cc * 32, v);
                 }
             }
             // accumulator drained: hand it back to the MMA warp

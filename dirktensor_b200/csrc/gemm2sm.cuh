@@ -43,6 +43,7 @@ struct __align__(1024) Smem {
     uint64_t acc_empty[kAccs];    // leader: both CTAs drained the accumulator
     uint64_t mma_done;
     uint32_t tmem_base;
+    alignas(128) float stage[4][32 * 32];  // epilogue: one 32 x 32 fp32 block per epilogue warp
 };
 
 enum : unsigned { kSiteEmpty = 0x41, kSiteFull, kSiteAcc, kSiteDone, kSiteAccEmpty };
@@ -268,12 +269,16 @@ gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
                     }
                 }
             } else {
+                const uint32_t stage = smem_u32(sm.stage[q]);
 #pragma unroll 1
                 for (int cc = 0; cc < kBN / 32; ++cc) {
                     float v[32];
                     tmem_ld32(taddr + cc * 32, v);
                     tmem_wait_ld();
-                    dt::gemm::store_chunk(p, row, n0 + cc * 32, v);
+                    if (dt::gemm::staged_f32(p, n0 + cc * 32))
+                        dt::gemm::store_rows_f32_staged(p, stage, row - lane, n0 + cc * 32, v, lane);
+                    else
+                        dt::gemm::store_chunk(p, row, n0 + cc * 32, v);
                 }
             }
             tc_fence_before();
