@@ -470,6 +470,46 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
                     *d4 = make_uint4(a, bb, c2, d);
                 }
             }
+        } else if (have_o && p.scatter_ranks == 0) {
+            // fp32 rows leave through the same quarter of the Q buffer, 64 columns (256 B
+            // of each row) at a time: each store instruction then writes two whole
+            // 256-byte row segments instead of 32 scattered 16-byte pieces.
+            tc_fence_after();
+            const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+            const float mul = row_valid ? inv_l : 0.f;
+            const uint32_t stage = smem_u32(sm.q[i]) + (uint32_t)(warp & 3) * 8192;
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+                for (int c2 = 0; c2 < 2; ++c2) {
+                    float o[32];
+                    tmem_ld32(tO + half * 64 + c2 * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {  // 16-byte chunk 8*c2+m of this row, XOR-swizzled by row
+                        const uint32_t chunk = (uint32_t)(8 * c2 + m) ^ (uint32_t)(lane & 15);
+                        st_shared_v4(stage + (uint32_t)lane * 256 + chunk * 16, __float_as_uint(o[4 * m] * mul),
+                                     __float_as_uint(o[4 * m + 1] * mul), __float_as_uint(o[4 * m + 2] * mul),
+                                     __float_as_uint(o[4 * m + 3] * mul));
+                    }
+                }
+                __syncwarp();
+#pragma unroll 4
+                for (int step = 0; step < 16; ++step) {
+                    const int rr = 2 * step + (lane >> 4);  // row within this warp's 32
+                    const uint32_t chunk = (uint32_t)(lane & 15);
+                    const int t = qt + (warp & 3) * 32 + rr;
+                    float4 x;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                                 : "r"(stage + (uint32_t)rr * 256 + ((chunk ^ (uint32_t)(rr & 15)) << 4)));
+                    if (t < p.T)
+                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) +
+                                                   ((long long)b * p.T + t) * p.out_row_stride + (long long)h * kD +
+                                                   half * 64 + chunk * 4) = x;
+                }
+                __syncwarp();  // the next half reuses the stage
+            }
         } else if (have_o) {
             tc_fence_after();
             const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
