@@ -130,6 +130,34 @@ __device__ __forceinline__ void store_row_chunk(float* base, const Params& p, in
     for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
+// Coalesced form of store_row_chunk for a warp: lane i holds row t0 + i.  The 32 x 32
+// block passes through `stage` (4 KB of shared memory owned by this warp; 16-byte chunk
+// j of row r at position j ^ (r & 7), so writes and reads use every bank), then each
+// store instruction writes four whole 128-byte row segments.  Rows t >= T are skipped.
+__device__ __forceinline__ void store_rows_staged(float* base, const Params& p, int b, int t0, int h, int col0,
+                                                  const float (&v)[32], uint32_t stage, int lane) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(stage + (uint32_t)lane * 128 +
+                                                                      ((uint32_t)(j ^ (lane & 7)) << 4)),
+                     "f"(v[4 * j]), "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                     : "memory");
+    __syncwarp();
+    const int j = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = 4 * i + (lane >> 3);
+        float4 x;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                     : "r"(stage + (uint32_t)r * 128 + ((uint32_t)(j ^ (r & 7)) << 4)));
+        const int t = t0 + r;
+        if (t < p.T)
+            *reinterpret_cast<float4*>(base + (((long long)b * p.T + t) * p.H + h) * kD + col0 + 4 * j) = x;
+    }
+    __syncwarp();  // the next block reuses the stage
+}
+
 // K-major operand (128 rows x 128 dims in two 64-dim halves), 16-wide K step kk.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int kk) {
     return umma_desc_sw128(tile + (uint32_t)((kk >> 2) * kHalfBytes + (kk & 3) * 32), 16, 1024);
@@ -419,18 +447,20 @@ attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_co
             if (lane == 0) mbar_arrive(&sm.pds_full);
         }
         // ---- epilogue: dK, dV rows of this key block -------------------------
-        if (ok && nq > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc)) {
+        bool got = ok && nq > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc);
+        got = __all_sync(0xffffffffu, got);  // the staged stores synchronise the warp
+        if (got) {
             tc_fence_after();
+            // every product has completed: the Q ring is idle and stages the rows (4 KB per warp)
+            const uint32_t stage = smem_u32(sm.q[0]) + (uint32_t)warp * 4096;
 #pragma unroll 1
             for (int cc = hf * 2; cc < hf * 2 + 2; ++cc) {
                 float a[32], bq[32];
                 tmem_ld32(tdK + lane_off + cc * 32, a);
                 tmem_ld32(tdV + lane_off + cc * 32, bq);
                 tmem_wait_ld();
-                if (k_pos < p.T) {
-                    store_row_chunk(p.dk, p, b, k_pos, h, cc * 32, a);
-                    store_row_chunk(p.dv, p, b, k_pos, h, cc * 32, bq);
-                }
+                store_rows_staged(p.dk, p, b, k_pos - lane, h, cc * 32, a, stage, lane);
+                store_rows_staged(p.dv, p, b, k_pos - lane, h, cc * 32, bq, stage, lane);
             }
         } else if (nq == 0 && k_pos < p.T) {
             float z[32];
@@ -682,14 +712,18 @@ attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_cons
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.ds_full);
         }
-        if (ok && nk > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc)) {
+        bool got = ok && nk > 0 && mbar_wait(&sm.acc_done, 0, kSiteAcc);
+        got = __all_sync(0xffffffffu, got);  // the staged stores synchronise the warp
+        if (got) {
             tc_fence_after();
+            // every product has completed: the Q tile is idle and stages the rows (4 KB per warp)
+            const uint32_t stage = smem_u32(sm.q) + (uint32_t)warp * 4096;
 #pragma unroll 1
             for (int cc = hf * 2; cc < hf * 2 + 2; ++cc) {
                 float a[32];
                 tmem_ld32(tdQ + lane_off + cc * 32, a);
                 tmem_wait_ld();
-                if (q_pos < p.T) store_row_chunk(p.dq, p, b, q_pos, h, cc * 32, a);
+                store_rows_staged(p.dq, p, b, q_pos - lane, h, cc * 32, a, stage, lane);
             }
         }
     }

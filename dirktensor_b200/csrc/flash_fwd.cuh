@@ -421,6 +421,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         const bool row_valid = q_pos < Tb;
         bool have_o = false;
         if (n > 0 && ok) have_o = mbar_wait_sleep(&sm.o_full[i], 0, kSiteO);
+        // the staged epilogues below synchronise the warp: take them only if every lane
+        // saw the accumulator (a wait that timed out on some lane is already reported)
+        have_o = __all_sync(0xffffffffu, have_o);
         if (have_o && p.out_bf16) {
             // bf16 rows leave through shared memory so that global (or peer)
             // stores are coalesced: each warp stages its 32 rows (256 B each) in
