@@ -378,7 +378,8 @@ attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_co
             const int s = it & 1;
             const int i = i0 + it;
             float pr[2][32];
-            if (!mbar_wait(&sm.s_full, it & 1, kSiteS)) { ok = false; break; }
+            // warp-uniform waits: each phase synchronises the warp
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, it & 1, kSiteS))) { ok = false; break; }
             tc_fence_after();
             const bool diag = p.causal && (i == kb);
             // both 32-column loads in flight before the one wait; then S^T's
@@ -410,7 +411,7 @@ attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_co
                     for (int e = 0; e < 32; ++e)
                         if (ch * 32 + e < rel) pr[ch][e] = 0.f;
             }
-            if (!mbar_wait(&sm.dp_full, it & 1, kSiteS)) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.dp_full, it & 1, kSiteS))) { ok = false; break; }
             tc_fence_after();
             // dP^T one 32-column chunk at a time (with both chunks and P live at
             // once the math warps ran out of registers and spilled).  Chunk ch of
@@ -667,7 +668,8 @@ attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_cons
         const float c = p.scale_log2;
         bool ok = true;
         for (int j = 0; j < nk; ++j) {
-            if (!mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1, kSiteS)) { ok = false; break; }
+            // warp-uniform waits: each phase synchronises the warp
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1, kSiteS))) { ok = false; break; }
             tc_fence_after();
             const int k0 = j * kBM;
             const bool masked = (p.causal && j == qb) || (k0 + kBM > p.T);
@@ -692,7 +694,7 @@ attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_cons
                     for (int e = 0; e < 32; ++e)
                         if (ch * 32 + e > lim) pr[ch][e] = 0.f;
             }
-            if (!mbar_wait(&sm.dp_full, j & 1, kSiteS)) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.dp_full, j & 1, kSiteS))) { ok = false; break; }
             tc_fence_after();
             float dp[2][32];
             tmem_ld32(tdP + lane_off + hf * 64, dp[0]);

@@ -329,7 +329,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         float m_run = -INFINITY, l_run = 0.f, mx = -INFINITY;
         bool ok = true;
         for (int j = 0; j < n; ++j) {
-            if (!mbar_wait_sleep(&sm.s_full[i], j & 1, kSiteS)) { ok = false; break; }
+            // warp-uniform, since the step synchronises the warp (__any_sync, __syncwarp)
+            if (!__all_sync(0xffffffffu, mbar_wait_sleep(&sm.s_full[i], j & 1, kSiteS))) { ok = false; break; }
             tc_fence_after();
             float s[128];
             tmem_ld32(tS + 0, *reinterpret_cast<float(*)[32]>(s + 0));

@@ -235,7 +235,9 @@ gemm_bf16_tn_2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
             ++it;
-            if (!mbar_wait(&sm.acc_full[acc], acc_phase, kSiteAcc)) break;
+            // warp-uniform: the staged stores below synchronise the warp (a lane whose
+            // wait expired has recorded the error; the whole warp stops)
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.acc_full[acc], acc_phase, kSiteAcc))) break;
             tc_fence_after();
             const uint32_t taddr = tmem + lane_off + acc * kBN;
             if (p.epilogue == dt::gemm::kSwiGLU) {
