@@ -138,3 +138,33 @@ def test_head_parallel_entry_points_validate_before_any_device_work():
     assert st == 1 and b"heads" in L.dt_last_error()
     assert L.dt_cast2_f32_bf16(None, None, None, None, 6, None) == 1
     assert L.dt_cast2_f32_bf16(None, None, None, None, 0, None) == 0
+
+
+def test_gemm_backward_and_noalloc_validate_before_device():
+    """The general and planar GEMM forms, the attention backward and the no-alloc
+    forward reject bad shapes, strides, alignments and sizes before any CUDA call."""
+    L = _lib.lib()
+    fake = 1 << 20  # 16-byte aligned, never dereferenced
+    # general form: bad c_mode, K not a multiple of 8 with a K-major operand, MN-major M % 8
+    assert L.dt_gemm_bf16(fake, 0, fake, 0, fake, 3, 16, 16, 64, 16, None) == 1
+    assert L.dt_gemm_bf16(fake, 0, fake, 0, fake, 0, 16, 16, 12, 16, None) == 1
+    assert L.dt_gemm_bf16(fake, 1, fake, 1, fake, 0, 12, 16, 64, 16, None) == 1
+    # ldc shorter than N, or leaving fp32 rows unaligned
+    assert L.dt_gemm_bf16_tn(fake, fake, fake, 0, 16, 16, 64, 8, None) == 1
+    assert L.dt_gemm_bf16_tn(fake, fake, fake, 0, 16, 16, 64, 18, None) == 1
+    # unaligned operand
+    assert L.dt_gemm_bf16_tn(fake + 4, fake, fake, 0, 16, 16, 64, 16, None) == 1
+    # planar A: K must split into planes of a multiple of 64
+    st = L.dt_gemm_bf16_tn_planar(fake, 3, fake, fake, 0, 16, 16, 2048, 16, None)
+    assert st == 1 and b"planes" in L.dt_last_error()
+    assert L.dt_gemm_bf16_tn_planar(fake, 4, fake, fake, 0, 16, 16, 96, 16, None) == 1
+    # attention backward: head_dim, then a workspace too small for the shape
+    st = L.dt_flash_bwd(*([None] * 10), 1, 16, 2, 64, 0.1, 1, None, 0, None)
+    assert st == 4 and b"head_dim" in L.dt_last_error()
+    ptrs = [fake] * 10
+    st = L.dt_flash_bwd(*ptrs, 1, 16, 2, 128, 0.1, 1, fake, 64, None)
+    assert st == 1 and b"workspace" in L.dt_last_error()
+    assert L.dt_flash_bwd(*([None] * 10), 0, 16, 2, 128, 0.1, 1, None, 0, None) == 0  # empty: no-op
+    # no-alloc forward: beyond its fixed scratch
+    st = L.dt_flash_fwd_noalloc(fake, fake, fake, fake, None, None, 2, 4096, 16, 128, 0.1, 1, None)
+    assert st == 1 and b"fixed scratch" in L.dt_last_error()
